@@ -1,0 +1,583 @@
+#!/usr/bin/env python
+"""Benchmark of the fused residual-add + RMSNorm hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload sweep|config0|shard|decode|relu]
+
+Prints ONE JSON line (rank 0).  Default workload ("sweep", BASELINE config 1,
+the configuration the headline metric is quoted on): one step is one pass of
+the fused op over batch 4096 bf16 at each of the 20 hidden sizes
+1024..16384 (step 1024), 20480, 24576, 28672, 32768.  `value` is the
+whole-job algorithmic HBM throughput in GB/s (bytes = 4*B*H*2 + 2*H per
+launch: read input, residual, weight; write output, residual) with inputs
+resident in HBM; `e2e` is the same metric through the C ABI with host
+buffers, the host<->device copies inside the timed region.
+
+Cold L2: every hidden size has its own buffers (4 GB per step in total, far
+above the 126 MB L2), so each launch's data was last touched one full step
+earlier; no flush is needed and nothing is cached between timed launches.
+
+Multi-GPU (torchrun, one process per GPU): rows shard with no collective;
+each rank runs the same per-GPU workload (weak scaling) and the step time is
+the max over ranks.  `--workload shard` instead splits BASELINE config 4's
+global batches (65536 x 8192 and 32768 x 32768) across the ranks (strong
+scaling).
+
+`--impl reference` times the reference's own CPU formula (the eager PyTorch
+expression of its test, test/test_hp_rms_norm.py:6-19, restated in
+oracle/oracle.py) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+SWEEP = [1024 * i for i in range(1, 17)] + [20480, 24576, 28672, 32768]
+BATCH = 4096
+ELEM = 2  # bytes per bf16 element
+METRIC = "fused add+RMSNorm µs and achieved HBM GB/s (% of B200 peak), batch 4096 bf16"
+# Reference README B200 table (CUDA 13.1 build, batch 4096 bf16), hp_rms_norm column, in us.
+README_US = {1024: 9.34, 2048: 12.35, 3072: 15.23, 4096: 18.69, 5120: 23.78, 6144: 28.8,
+             7168: 34.69, 8192: 39.9, 9216: 46.43, 10240: 51.42, 11264: 55.14, 12288: 59.78,
+             13312: 80.38, 14336: 83.39, 15360: 86.4, 16384: 90.98, 20480: 115.74,
+             24576: 137.31, 28672: 161.15, 32768: 182.34}
+SHARD_SHAPES = [(65536, 8192), (32768, 32768)]
+DECODE_ROWS = [1, 7, 33, 128, 512]
+DECODE_HIDDEN = [4096, 5120, 7168, 8192]
+RELU_SHAPES = [((4096, 14336), "bf16"), ((8192, 28672), "fp16")]
+
+
+def alg_bytes(rows: int, hidden: int) -> int:
+    return 4 * rows * hidden * ELEM + hidden * ELEM
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["sweep", "config0", "shard", "decode", "relu"],
+                    default="sweep")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU work budget of the cpu_baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--out", default=None, help="also write the JSON line to this file")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return args
+
+
+# --------------------------------------------------------------------------
+# Distributed plumbing (one process per GPU; no collective on the data path).
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+
+    def init(self, backend: str):
+        import torch.distributed as dist
+
+        if self.world > 1 and not dist.is_initialized():
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=180))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, v: float, device=None) -> float:
+        if not self.pg:
+            return v
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------
+# Clock sampling during the timed region (NVML reads only).
+
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.dev = device_index
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.error = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = None
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
+            except Exception:
+                pass
+            h = None
+            if uuid:
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+                except Exception:
+                    h = None
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+            self._h = h
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # no NVML: report what we could not sample
+            self.error = f"{type(e).__name__}: {e}"
+        return self
+
+    def _run(self):
+        nv, h = self._nv, self._h
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception as e:
+                self.error = str(e)
+                return
+            time.sleep(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        out = {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+               "sm_max_mhz": self.max_mhz,
+               "reasons": [n for b, n in self.REASONS.items() if self.reasons & b and b != 0x1],
+               "samples": len(self.samples), "source": "nvml"}
+        if self.error:
+            out["error"] = self.error
+        return out
+
+
+# --------------------------------------------------------------------------
+# Measurement helpers.
+
+def measured_peak():
+    """Measured HBM copy bandwidth of this pool (driver-written), else fallback."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback (6.65 TB/s)"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes from the committed ncu summary, keyed by hidden size."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+def make_rows(rows, hidden, dtype, device, seed):
+    """BASELINE config-0 distributions, generated on the device from a seed."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(rows, hidden, generator=g, device=device, dtype=torch.float32).to(dtype)
+    r = torch.randn(rows, hidden, generator=g, device=device, dtype=torch.float32).to(dtype)
+    w = (1.0 + 0.1 * torch.randn(hidden, generator=g, device=device)).to(dtype)
+    return x, w, r
+
+
+def cpu_eager_sample(shapes, seconds: float):
+    """Times the reference formula on the host cores over a bounded sample.
+
+    Returns (GB/s, description, threads)."""
+    import torch
+
+    from oracle import oracle as O
+
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(0)
+    data = []
+    for rows, hidden in shapes:
+        x = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+        r = torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
+        w = (1.0 + 0.1 * torch.randn(hidden, generator=g)).to(torch.bfloat16)
+        data.append((x, w, r))
+    x0, w0, r0 = data[0]
+    O.eager_formula(x0, r0, w0, 1e-6)  # warm the thread pool
+    total_bytes, t0, passes = 0, time.perf_counter(), 0
+    while True:
+        for (x, w, r), (rows, hidden) in zip(data, shapes):
+            O.eager_formula(x, r, w, 1e-6)
+            total_bytes += alg_bytes(rows, hidden)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return total_bytes / el / 1e9, passes, threads
+
+
+# --------------------------------------------------------------------------
+# Our implementation.
+
+def run_ours(args, dist):
+    import torch
+
+    from hp_rms_norm_b200 import capi
+
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    dist.init("nccl")
+    capi.load()
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+
+    # ---- problem list for one step --------------------------------------
+    scaling = "weak"
+    if args.workload == "sweep":
+        shapes = [(BATCH, h) for h in SWEEP]
+        workload = ("config1: fused add+RMSNorm hidden sweep 1024..16384 step 1024 + 20480, "
+                    "24576, 28672, 32768 at batch 4096 bf16 (20 launches per step)")
+    elif args.workload == "config0":
+        shapes = [(BATCH, 4096)]
+        workload = "config0: fused add+RMSNorm 4096 x 4096 bf16"
+    elif args.workload == "shard":
+        scaling = "strong"
+        shapes = []
+        for rows, h in SHARD_SHAPES:
+            per = rows // dist.world
+            shapes.append((per + (1 if dist.rank < rows % dist.world else 0), h))
+        workload = ("config4: global 65536 x 8192 and 32768 x 32768 bf16, rows split evenly "
+                    "across ranks, no collective")
+    elif args.workload == "decode":
+        shapes = [(r, h) for r in DECODE_ROWS for h in DECODE_HIDDEN]
+        workload = "config2 shapes (bf16): rows {1,7,33,128,512} x hidden {4096,5120,7168,8192}"
+    else:
+        return run_relu(args, dist, dev, stream)
+
+    bufs = []
+    for i, (rows, h) in enumerate(shapes):
+        x, w, r = make_rows(rows, h, torch.bfloat16, dev, seed=1000 * dist.rank + i)
+        bufs.append((x, w, r))
+    plans = [capi.plan(rows, h, capi.DTYPE_BF16, x.data_ptr(), r.data_ptr())
+             for (rows, h), (x, w, r) in zip(shapes, bufs)]
+    step_bytes = sum(alg_bytes(rows, h) for rows, h in shapes)
+    eps = 1e-6
+
+    def one_step(evs=None):
+        for i, ((rows, h), (x, w, r)) in enumerate(zip(shapes, bufs)):
+            if evs is not None:
+                evs[i][0].record(stream)
+            capi.rms_norm(x.data_ptr(), w.data_ptr(), r.data_ptr(), rows, h, h, h, eps,
+                          capi.DTYPE_BF16, sh)
+            if evs is not None:
+                evs[i][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            one_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    K = args.steps
+    inner = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in shapes] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        torch.cuda.synchronize()
+        dist.barrier()
+        start.record(stream)
+        for k in range(K):
+            one_step(inner[k])
+        end.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    elapsed_ms = dist.max(start.elapsed_time(end), dev)
+    ms_per_step = elapsed_ms / K
+    value = dist.world * step_bytes * K / (elapsed_ms / 1e3) / 1e9 if scaling == "weak" else \
+        sum(alg_bytes(r, h) for r, h in
+            (SHARD_SHAPES if args.workload == "shard" else shapes)) * K / (elapsed_ms / 1e3) / 1e9
+
+    # ---- per-shape breakdown and roofline of the dominant kernel ----------
+    peak, peak_src = measured_peak()
+    per_shape, by_plan = [], {}
+    for i, ((rows, h), plan) in enumerate(zip(shapes, plans)):
+        us = statistics.median(inner[k][i][0].elapsed_time(inner[k][i][1]) for k in range(K)) * 1e3
+        b = alg_bytes(rows, h)
+        entry = {"rows": rows, "hidden": h, "us": round(us, 2), "gbs": round(b / us / 1e3, 1),
+                 "frac": round(b / us / 1e3 / peak, 3), "plan": plan}
+        if args.workload == "sweep" and h in README_US:
+            entry["readme_us"] = README_US[h]
+        per_shape.append(entry)
+        kern = plan.split(":tpr")[0]
+        t, bb, n = by_plan.get(kern, (0.0, 0, 0))
+        by_plan[kern] = (t + us, bb + b, n + 1)
+    dom = max(by_plan, key=lambda k: by_plan[k][0])
+    t_us, b_dom, n_dom = by_plan[dom]
+    achieved = b_dom / t_us / 1e3
+    traffic = None
+    tr = committed_traffic()
+    if tr:
+        vals = [tr.get(str(e["hidden"])) for e in per_shape if e["plan"].startswith(dom)]
+        if vals and all(v is not None for v in vals):
+            traffic = int(sum(vals) / len(vals))
+    roofline = {"bound": "hbm", "kernel": dom, "launches_per_step": n_dom,
+                "time_share": round(t_us / sum(v[0] for v in by_plan.values()), 3),
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 3), "peak_source": peak_src,
+                "algorithmic_bytes_per_launch": int(b_dom / n_dom), "traffic": traffic}
+
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": dist.world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded on device: input, residual ~ N(0,1), weight ~ N(1,0.1), "
+                    "eps 1e-6)",
+            "config": {"workload": workload, "batch": BATCH if args.workload != "decode" else None,
+                       "shapes": [list(s) for s in shapes],
+                       "l2": "cold: separate buffers per shape, 4 GB touched per step >> 126 MB L2",
+                       "bytes_per_step": step_bytes, "parallelism": f"rows sharded x{dist.world}, "
+                       "no collective"},
+            "frac_of_peak": round(value / dist.world / peak, 3),
+            "gpu_launches": K * len(shapes),
+            "roofline": roofline, "per_shape": per_shape,
+            "clocks": clocks.summary()}
+    if args.workload == "sweep":
+        readme_gbs = sum(alg_bytes(BATCH, h) for h in SWEEP) / (sum(README_US.values()) * 1e3)
+        line["vs_baseline"] = round(value / dist.world / readme_gbs, 3)
+        line["baseline_note"] = ("vs_baseline = per-GPU value / the reference README's B200 "
+                                 f"aggregate over the same 20 shapes ({readme_gbs:.1f} GB/s, "
+                                 "README.md:13-32, CUDA 13.1, L2 state unstated)")
+
+    # ---- end to end through the C ABI with host buffers --------------------
+    if not args.no_e2e and args.workload in ("sweep", "config0", "shard"):
+        line["e2e"] = run_e2e(args, shapes, bufs, stream, dev, dist, eps)
+
+    # ---- CPU baseline (rank 0, N = 1) --------------------------------------
+    if dist.world == 1 and not args.no_cpu_baseline:
+        sample_rows = 128
+        gbs, passes, threads = cpu_eager_sample([(sample_rows, h) for _, h in shapes],
+                                                args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": (f"reference eager formula (test/test_hp_rms_norm.py:6-19) on {threads} "
+                       f"host threads, {sample_rows} rows at each of the {len(shapes)} shapes, "
+                       f"{passes} passes (~{args.cpu_seconds:.0f} s)")}
+    return line
+
+
+def run_e2e(args, shapes, bufs, stream, dev, dist, eps):
+    """Same metric through the C ABI with pinned host buffers: per step, every
+    shape's input, residual and weight go host->device, the kernel runs, and the
+    output and residual come back device->host.  Chunks of rows rotate over
+    three streams so the two copy directions overlap."""
+    import torch
+
+    from hp_rms_norm_b200 import capi
+
+    host = []
+    for (rows, h), (x, w, r) in zip(shapes, bufs):
+        host.append((x.cpu().pin_memory(), w.cpu().pin_memory(), r.cpu().pin_memory(),
+                     torch.empty_like(x, device="cpu").pin_memory(),
+                     torch.empty_like(r, device="cpu").pin_memory()))
+    streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
+    chunk_bytes = 32 << 20
+    h2d = sum(x.numel() * 2 + r.numel() * 2 + w.numel() * 2 for x, w, r in bufs)
+    d2h = sum(x.numel() * 2 + r.numel() * 2 for x, w, r in bufs)
+
+    def step():
+        c = 0
+        for (rows, h), (x, w, r), (hx, hw, hr, ox, orr) in zip(shapes, bufs, host):
+            per = max(1, chunk_bytes // (h * 2 * 2))
+            w.copy_(hw, non_blocking=True)
+            for s in streams:
+                s.wait_stream(torch.cuda.current_stream())
+            for r0 in range(0, rows, per):
+                r1 = min(rows, r0 + per)
+                s = streams[c % len(streams)]
+                c += 1
+                with torch.cuda.stream(s):
+                    x[r0:r1].copy_(hx[r0:r1], non_blocking=True)
+                    r[r0:r1].copy_(hr[r0:r1], non_blocking=True)
+                    capi.rms_norm(x[r0:r1].data_ptr(), w.data_ptr(), r[r0:r1].data_ptr(), r1 - r0,
+                                  h, h, h, eps, capi.DTYPE_BF16, s.cuda_stream)
+                    ox[r0:r1].copy_(x[r0:r1], non_blocking=True)
+                    orr[r0:r1].copy_(r[r0:r1], non_blocking=True)
+            for s in streams:
+                torch.cuda.current_stream().wait_stream(s)
+
+    for _ in range(1):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    K = max(1, args.e2e_steps)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(K):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = dist.max(t0.elapsed_time(t1), dev) / K
+    total = sum(alg_bytes(rows, h) for rows, h in shapes) * dist.world
+    return {"value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
+            "steps": K, "api": "hprn_rms_norm (C ABI) on pinned-host-staged buffers, 3 streams"}
+
+
+def run_relu(args, dist, dev, stream):
+    import torch
+
+    from hp_rms_norm_b200 import capi
+
+    bufs = []
+    for (shape, dt) in RELU_SHAPES:
+        tdt = torch.bfloat16 if dt == "bf16" else torch.float16
+        g = torch.Generator(device=dev).manual_seed(3 + dist.rank)
+        x = torch.randn(shape, generator=g, device=dev).to(tdt)
+        bufs.append((x, torch.empty_like(x), capi.DTYPE_BF16 if dt == "bf16" else capi.DTYPE_FP16))
+    step_bytes = sum(2 * x.numel() * 2 for x, _, _ in bufs)
+
+    def one_step():
+        for x, o, code in bufs:
+            capi.relu(o.data_ptr(), x.data_ptr(), x.shape[0], x.shape[1], x.shape[1], x.shape[1],
+                      code, stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            one_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            one_step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = dist.max(start.elapsed_time(end), dev) / args.steps
+    peak, src = measured_peak()
+    value = dist.world * step_bytes / (ms / 1e3) / 1e9
+    return {"metric": "elementwise ReLU achieved HBM GB/s", "value": round(value, 1),
+            "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16+fp16", "data": "synthetic N(0,1)",
+            "config": {"workload": "config3: relu bf16 (4096,14336) + fp16 (8192,28672)",
+                       "l2": "inputs 112 MiB + 448 MiB per step"},
+            "roofline": {"bound": "hbm", "achieved": round(value / dist.world, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(value / dist.world / peak, 3),
+                         "peak_source": src, "traffic": None},
+            "gpu_launches": args.steps * len(bufs), "clocks": clocks.summary()}
+
+
+# --------------------------------------------------------------------------
+# The reference arm: the reference's CPU formula on the host cores.
+
+def run_reference(args, dist):
+    import torch
+
+    if dist.rank != 0:
+        return None
+    shapes = [(BATCH, h) for h in SWEEP] if args.workload == "sweep" else [(BATCH, 4096)]
+    sample_rows = 64
+    sample = [(sample_rows, h) for _, h in shapes]
+    g = torch.Generator().manual_seed(0)
+    from oracle import oracle as O
+
+    data = []
+    for rows, h in sample:
+        x = torch.randn(rows, h, generator=g).to(torch.bfloat16)
+        r = torch.randn(rows, h, generator=g).to(torch.bfloat16)
+        w = (1.0 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)
+        data.append((x, w, r))
+    step_bytes = sum(alg_bytes(rows, h) for rows, h in sample)
+
+    def step():
+        for x, w, r in data:
+            O.eager_formula(x, r, w, 1e-6)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = step_bytes * args.steps / el / 1e9
+    threads = torch.get_num_threads()
+    desc = (f"reference eager formula (test/test_hp_rms_norm.py:6-19, restated in oracle/oracle.py) "
+            f"on {threads} host threads; each step = {sample_rows} rows at each of the "
+            f"{len(shapes)} shapes of the workload")
+    return {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": ("config1 hidden sweep, batch 4096 bf16 (sampled)"
+                                    if args.workload == "sweep" else args.workload),
+                       "sample_rows_per_shape": sample_rows},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                             "kind": "port", "sample": desc},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse_args()
+    dist = Dist()
+    if args.impl == "reference":
+        line = run_reference(args, dist)
+    else:
+        line = run_ours(args, dist)
+    if line is not None and dist.rank == 0:
+        s = json.dumps(line)
+        print(s, flush=True)
+        if args.out:
+            with open(args.out, "w") as f:
+                f.write(s + "\n")
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

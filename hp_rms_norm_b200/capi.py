@@ -1,0 +1,142 @@
+"""ctypes binding of the C ABI (include/hp_rms_norm_b200.h).
+
+This is what a non-torch caller would bind, and what the GPU parity tests call:
+plain device pointers, element counts, row strides, a dtype code and a
+``cudaStream_t`` as an integer.  Errors raise ``HprnError`` carrying the
+library's status code and message.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libhp_rms_norm_b200.so")
+
+DTYPE_BF16 = 0
+DTYPE_FP16 = 1
+
+OK = 0
+ERR_INVALID_ARGUMENT = -1
+ERR_UNSUPPORTED_DTYPE = -2
+ERR_UNSUPPORTED_DEVICE = -3
+ERR_CUDA = -4
+
+# Every symbol include/hp_rms_norm_b200.h declares.
+EXPORTED = (
+    "hprn_rms_norm",
+    "hprn_relu",
+    "hprn_last_error",
+    "hprn_status_string",
+    "hprn_version",
+    "hprn_rms_norm_plan",
+    "hprn_set_plan_override",
+)
+
+
+class HprnError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} (status {status})")
+        self.status = status
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads the C-ABI library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise ImportError(
+            f"{path} is missing: build it with `python -m hp_rms_norm_b200.build` "
+            "(the CUDA library is required; there is no CPU fallback)")
+    lib = ctypes.CDLL(path)
+    vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    lib.hprn_rms_norm.argtypes = [vp, vp, vp, i64, i64, i64, i64, ctypes.c_double, c_int, vp]
+    lib.hprn_rms_norm.restype = c_int
+    lib.hprn_relu.argtypes = [vp, vp, i64, i64, i64, i64, c_int, vp]
+    lib.hprn_relu.restype = c_int
+    lib.hprn_last_error.argtypes = []
+    lib.hprn_last_error.restype = ctypes.c_char_p
+    lib.hprn_status_string.argtypes = [c_int]
+    lib.hprn_status_string.restype = ctypes.c_char_p
+    lib.hprn_version.argtypes = []
+    lib.hprn_version.restype = c_int
+    lib.hprn_rms_norm_plan.argtypes = [i64, i64, c_int, vp, vp, i64, i64, ctypes.c_char_p, c_int]
+    lib.hprn_rms_norm_plan.restype = c_int
+    lib.hprn_set_plan_override.argtypes = [ctypes.c_char_p]
+    lib.hprn_set_plan_override.restype = c_int
+    _lib = lib
+    return lib
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        lib = load()
+        raise HprnError(status, lib.hprn_last_error().decode())
+
+
+def rms_norm(input_ptr: int, weight_ptr: int, residual_ptr: int, rows: int, hidden: int,
+             input_row_stride: int, residual_row_stride: int, eps: float, dtype: int,
+             stream: int = 0) -> None:
+    _check(load().hprn_rms_norm(input_ptr, weight_ptr, residual_ptr, rows, hidden,
+                                input_row_stride, residual_row_stride, eps, dtype, stream))
+
+
+def relu(out_ptr: int, input_ptr: int, rows: int, hidden: int, out_row_stride: int,
+         input_row_stride: int, dtype: int, stream: int = 0) -> None:
+    _check(load().hprn_relu(out_ptr, input_ptr, rows, hidden, out_row_stride, input_row_stride,
+                            dtype, stream))
+
+
+def plan(rows: int, hidden: int, dtype: int = DTYPE_BF16, input_ptr: int = 0,
+         residual_ptr: int = 0, input_row_stride: int | None = None,
+         residual_row_stride: int | None = None) -> str:
+    buf = ctypes.create_string_buffer(128)
+    xs = hidden if input_row_stride is None else input_row_stride
+    rs = hidden if residual_row_stride is None else residual_row_stride
+    _check(load().hprn_rms_norm_plan(rows, hidden, dtype, input_ptr, residual_ptr, xs, rs, buf, 128))
+    return buf.value.decode()
+
+
+def set_plan_override(plan_str: str | None) -> None:
+    _check(load().hprn_set_plan_override(plan_str.encode() if plan_str else None))
+
+
+def version() -> int:
+    return int(load().hprn_version())
+
+
+# --- torch conveniences (device pointers from tensors) ----------------------
+
+def dtype_code(t) -> int:
+    import torch
+
+    if t.dtype == torch.bfloat16:
+        return DTYPE_BF16
+    if t.dtype == torch.float16:
+        return DTYPE_FP16
+    raise HprnError(ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16")
+
+
+def rms_norm_tensors(inp, weight, res, eps: float, stream: int | None = None) -> None:
+    """C-ABI call on 2-D CUDA tensors (row stride from the tensors)."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(inp.device).cuda_stream
+    rows, hidden = inp.shape
+    rms_norm(inp.data_ptr(), weight.data_ptr(), res.data_ptr(), rows, hidden, inp.stride(0),
+             res.stride(0), eps, dtype_code(inp), stream)
+
+
+def relu_tensors(out, inp, stream: int | None = None) -> None:
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(inp.device).cuda_stream
+    rows, hidden = inp.shape
+    relu(out.data_ptr(), inp.data_ptr(), rows, hidden, out.stride(0), inp.stride(0),
+         dtype_code(inp), stream)

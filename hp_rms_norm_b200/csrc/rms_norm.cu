@@ -1,0 +1,736 @@
+// Fused residual-add + RMSNorm for sm_100a, and its C-ABI entry point.
+//
+// Per row i (hidden elements, 16-bit storage T, fp32 arithmetic):
+//   s_j   = f32(x_ij) + f32(r_ij)
+//   r_ij <- round_T(s_j)
+//   inv   = rsqrt(eps + sum_j s_j^2 / hidden)          (s_j before rounding)
+//   x_ij <- round_T(f32(r_ij) * f32(w_j) * inv)
+// which is the arithmetic of the reference kernel
+// (hp_rms_norm/csrc/cuda/hp_rms_norm.cuh:186-207 for the add and the sum of
+// squares, :231 for the inverse RMS, :104-110 for the output product).
+//
+// The work is purely HBM-bound (8 bytes moved per element, ~6 flops), so the
+// kernels are built to keep HBM busy:
+//   * every row is read from HBM exactly once and written exactly once: the
+//     rounded residual stays in registers between the sum-of-squares pass and
+//     the output pass;
+//   * all of a thread's loads are issued before any of them is consumed
+//     (VPT vectors of input and residual in flight per thread), with 256-bit
+//     ld/st.global.v8.b32 where alignment allows;
+//   * streamed rows are marked L2 evict_first, the weight row evict_last;
+//   * the row is split across 1 warp (short rows, no shared memory or block
+//     barrier at all), one CTA, or a thread-block cluster of up to 8 CTAs
+//     whose partial sums meet in distributed shared memory, so that CTAs stay
+//     small enough for many to be resident per SM at every hidden size (no
+//     occupancy cliff at large hidden, and short batches still spread over
+//     many SMs);
+//   * rows too long for the register-resident kernels use a two-pass kernel
+//     that re-reads its own just-written residual from L2, not HBM.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <string>
+
+#include "runtime.cuh"
+#include "vec.cuh"
+
+namespace hprn {
+
+struct RmsArgs {
+  uint16_t* x;         // input, overwritten with the output
+  const uint16_t* w;   // weight [hidden]
+  uint16_t* r;         // residual, overwritten with input + residual
+  int64_t rows;
+  int64_t x_stride;    // elements between rows
+  int64_t r_stride;
+  int32_t nvec;        // vectors per row (hidden / elements-per-vector)
+  int32_t slice_vecs;  // vectors per CTA when a cluster splits the row
+  int32_t rows_per_cta;
+  float eps;
+  float inv_hidden;
+};
+
+// Adds residual into input in fp32, keeps the rounded sum in `xv`, and
+// accumulates the squares of the unrounded sums.
+template <typename T, int VEC>
+__device__ __forceinline__ void add_round(Vec<VEC>& xv, const Vec<VEC>& rv, float& a0, float& a1) {
+  if constexpr (VEC == 2) {
+    const float s = unpack1<T>(xv.h) + unpack1<T>(rv.h);
+    a0 = fmaf(s, s, a0);
+    xv.h = pack1<T>(s);
+  } else {
+#pragma unroll
+    for (int k = 0; k < Vec<VEC>::kWords; ++k) {
+      const float2 a = unpack2<T>(xv.w[k]);
+      const float2 b = unpack2<T>(rv.w[k]);
+      const float s0 = a.x + b.x;
+      const float s1 = a.y + b.y;
+      a0 = fmaf(s0, s0, a0);
+      a1 = fmaf(s1, s1, a1);
+      xv.w[k] = pack2<T>(s0, s1);
+    }
+  }
+}
+
+// round_T((f32(r) * f32(w)) * inv), multiplied in the reference's order.
+template <typename T, int VEC>
+__device__ __forceinline__ Vec<VEC> normalize(const Vec<VEC>& rv, const Vec<VEC>& wv, float inv) {
+  Vec<VEC> o;
+  if constexpr (VEC == 2) {
+    o.h = pack1<T>(unpack1<T>(rv.h) * unpack1<T>(wv.h) * inv);
+  } else {
+#pragma unroll
+    for (int k = 0; k < Vec<VEC>::kWords; ++k) {
+      const float2 a = unpack2<T>(rv.w[k]);
+      const float2 b = unpack2<T>(wv.w[k]);
+      o.w[k] = pack2<T>(a.x * b.x * inv, a.y * b.y * inv);
+    }
+  }
+  return o;
+}
+
+// Butterfly sum: every lane ends with the same bits.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Stores `v` into the shared-memory word at `local` in CTA `rank` of this cluster.
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(local));
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 1: one warp per row (rows of at most 4 * 32 vectors).  No shared
+// memory, no block barrier: a warp that has finished its row retires without
+// waiting for the rest of its CTA.
+template <typename T, int VEC, int VPT>
+__global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
+  constexpr int EPV = Vec<VEC>::kElems;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  uint16_t* xr = a.x + row * a.x_stride;
+  uint16_t* rr = a.r + row * a.r_stride;
+  const uint64_t pol_stream = policy_evict_first();
+  const uint64_t pol_keep = policy_evict_last();
+
+  Vec<VEC> xv[VPT], rv[VPT], wv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = lane + 32 * j;
+    if (v < a.nvec) {
+      xv[j] = ld_stream<VEC>(xr + v * EPV, pol_stream);
+      rv[j] = ld_stream<VEC>(rr + v * EPV, pol_stream);
+    }
+  }
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = lane + 32 * j;
+    if (v < a.nvec) {
+      add_round<T, VEC>(xv[j], rv[j], a0, a1);
+      st_global<VEC>(rr + v * EPV, xv[j]);
+      wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
+    }
+  }
+  const float inv = rsqrtf(fmaf(warp_sum(a0 + a1), a.inv_hidden, a.eps));
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = lane + 32 * j;
+    if (v < a.nvec) st_global<VEC>(xr + v * EPV, normalize<T, VEC>(xv[j], wv[j], inv));
+  }
+}
+
+// Largest CTA a cta/cluster kernel with VPT vectors per thread is compiled
+// for: the register budget per thread (65536 / max threads) must hold the
+// 3 * VPT vectors in flight without spilling.
+__host__ __device__ constexpr int cta_max_threads(int vpt) {
+  return vpt <= 2 ? 1024 : (vpt <= 4 ? 512 : 256);
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2: one CTA per row slice; with CLUSTER, the row is split over the
+// CTAs of a thread-block cluster (launched with cluster dims (n, 1, 1)) and
+// the per-CTA partial sums of squares are pushed into every peer's shared
+// memory, so each CTA finishes the reduction locally after one cluster
+// barrier and no CTA touches a peer's memory afterwards.
+template <typename T, int VEC, int VPT, bool CLUSTER>
+__global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArgs a) {
+  constexpr int EPV = Vec<VEC>::kElems;
+  __shared__ float warp_part[32];
+  __shared__ float cta_part[8];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nthreads = blockDim.x;
+
+  int64_t row;
+  int v_begin = 0, v_end = a.nvec;
+  uint32_t crank = 0, csize = 1;
+  if constexpr (CLUSTER) {
+    // Phase 1 of the cluster barrier: completes once every CTA of the cluster
+    // is running, which makes their shared memory safe to write.
+    cluster_arrive_relaxed();
+    crank = cluster_ctarank();
+    csize = cluster_nctarank();
+    row = cluster_id_x();
+    v_begin = static_cast<int>(crank) * a.slice_vecs;
+    v_end = min(v_begin + a.slice_vecs, a.nvec);
+  } else {
+    row = blockIdx.x;
+  }
+  uint16_t* xr = a.x + row * a.x_stride;
+  uint16_t* rr = a.r + row * a.r_stride;
+  const uint64_t pol_stream = policy_evict_first();
+  const uint64_t pol_keep = policy_evict_last();
+
+  Vec<VEC> xv[VPT], rv[VPT], wv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = v_begin + tid + j * nthreads;
+    if (v < v_end) {
+      xv[j] = ld_stream<VEC>(xr + static_cast<int64_t>(v) * EPV, pol_stream);
+      rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
+    }
+  }
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = v_begin + tid + j * nthreads;
+    if (v < v_end) {
+      add_round<T, VEC>(xv[j], rv[j], a0, a1);
+      st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+      wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
+    }
+  }
+
+  const float wsum = warp_sum(a0 + a1);
+  if (lane == 0) warp_part[warp] = wsum;
+  __syncthreads();
+  float total = warp_sum(lane < (nthreads >> 5) ? warp_part[lane] : 0.f);
+  if constexpr (CLUSTER) {
+    cluster_wait();  // phase 1: all peers are running
+    if (warp == 0 && lane < static_cast<int>(csize)) st_cluster_f32(&cta_part[crank], lane, total);
+    cluster_arrive_release();
+    cluster_wait();  // phase 2: every CTA's partial has landed in every CTA
+    total = warp_sum(lane < static_cast<int>(csize) ? cta_part[lane] : 0.f);
+  }
+  const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = v_begin + tid + j * nthreads;
+    if (v < v_end) {
+      st_global<VEC>(xr + static_cast<int64_t>(v) * EPV, normalize<T, VEC>(xv[j], wv[j], inv));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 3: rows longer than the register-resident kernels hold.  Pass 1
+// streams input and residual from HBM, writes the rounded residual and sums
+// squares; pass 2 re-reads each thread's own residual vectors from L2 (.cg),
+// multiplies by the weight and writes the output.
+constexpr int kTwoPassThreads = 512;
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) {
+  constexpr int EPV = Vec<VEC>::kElems;
+  constexpr int U = 4;
+  __shared__ float warp_part[32];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nthreads = blockDim.x;
+  const int64_t row = blockIdx.x;
+  uint16_t* xr = a.x + row * a.x_stride;
+  uint16_t* rr = a.r + row * a.r_stride;
+  const uint64_t pol_stream = policy_evict_first();
+  const uint64_t pol_keep = policy_evict_last();
+
+  float a0 = 0.f, a1 = 0.f;
+  for (int base = 0; base < a.nvec; base += U * nthreads) {
+    Vec<VEC> xv[U], rv[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int v = base + tid + j * nthreads;
+      if (v < a.nvec) {
+        xv[j] = ld_stream<VEC>(xr + static_cast<int64_t>(v) * EPV, pol_stream);
+        rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int v = base + tid + j * nthreads;
+      if (v < a.nvec) {
+        add_round<T, VEC>(xv[j], rv[j], a0, a1);
+        st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+      }
+    }
+  }
+  const float wsum = warp_sum(a0 + a1);
+  if (lane == 0) warp_part[warp] = wsum;
+  __syncthreads();
+  const float total = warp_sum(lane < (nthreads >> 5) ? warp_part[lane] : 0.f);
+  const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
+
+  for (int base = 0; base < a.nvec; base += U * nthreads) {
+    Vec<VEC> sv[U], wv[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int v = base + tid + j * nthreads;
+      if (v < a.nvec) {
+        sv[j] = ld_l2<VEC>(rr + static_cast<int64_t>(v) * EPV);
+        wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int v = base + tid + j * nthreads;
+      if (v < a.nvec) {
+        st_global<VEC>(xr + static_cast<int64_t>(v) * EPV, normalize<T, VEC>(sv[j], wv[j], inv));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Launch plans.
+
+enum Kind { kWarpRows = 0, kCtaRows = 1, kClusterRows = 2, kTwoPass = 3 };
+
+struct Plan {
+  Kind kind = kWarpRows;
+  int vec = 32;          // bytes per vector
+  int vpt = 1;           // vectors per thread
+  int tpr = 32;          // threads per CTA working on one row slice
+  int cluster = 1;       // CTAs per row
+  int rows_per_cta = 1;  // warp kind only
+};
+
+const char* kind_name(Kind k) {
+  switch (k) {
+    case kWarpRows: return "warp";
+    case kCtaRows: return "cta";
+    case kClusterRows: return "cluster";
+    default: return "twopass";
+  }
+}
+
+std::string plan_string(const Plan& p) {
+  char buf[96];
+  snprintf(buf, sizeof(buf), "%s:vec%d:vpt%d:tpr%d:cluster%d:rpc%d", kind_name(p.kind), p.vec,
+           p.vpt, p.tpr, p.cluster, p.rows_per_cta);
+  return buf;
+}
+
+// VPT values compiled for each kind (must match the dispatch tables below).
+bool vpt_supported(Kind k, int vec, int vpt) {
+  switch (k) {
+    case kWarpRows: return vpt >= 1 && vpt <= 4;
+    case kCtaRows:
+    case kClusterRows:
+      if (vec == 32) return vpt == 1 || vpt == 2 || vpt == 3 || vpt == 4 || vpt == 6 || vpt == 8;
+      return vpt == 1 || vpt == 2 || vpt == 4 || vpt == 8;
+    default: return true;
+  }
+}
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+int next_supported_vpt(Kind k, int vec, int vpt) {
+  for (int v = vpt; v <= 8; ++v)
+    if (vpt_supported(k, vec, v)) return v;
+  return -1;
+}
+
+// Largest vector width every pointer, stride and the hidden size allow.
+int choose_vec(int64_t hidden, int64_t rows, const void* x, const void* r, const void* w,
+               int64_t xs, int64_t rs) {
+  for (int vec : {32, 16, 8, 4}) {
+    const int epv = vec / 2;
+    if (hidden % epv) continue;
+    if (!aligned(x, vec) || !aligned(r, vec) || !aligned(w, vec)) continue;
+    if (rows > 1 && (((xs * 2) % vec) || ((rs * 2) % vec))) continue;
+    return vec;
+  }
+  return 2;
+}
+
+Plan default_plan(int64_t rows, int nvec, int vec, const DeviceInfo& dev) {
+  Plan p;
+  p.vec = vec;
+  if (nvec <= 4 * 32) {
+    p.kind = kWarpRows;
+    p.vpt = next_supported_vpt(kWarpRows, vec, (nvec + 31) / 32);
+    p.tpr = 32;
+    p.rows_per_cta = 4;
+    return p;
+  }
+  // One CTA (or cluster) per row: two vectors per thread, at most 256 threads
+  // per CTA, with the row split over a cluster once a CTA would exceed that.
+  int vpt = 2, cluster = 1;
+  auto per_cta_threads = [&](int c, int v) { return ((nvec + c - 1) / c + v - 1) / v; };
+  while (per_cta_threads(cluster, vpt) > 256 && cluster < 8) cluster *= 2;
+  // Short batches: spread rows over more SMs while each CTA keeps >= 2 warps of work.
+  while (rows * cluster < dev.sm_count && cluster < 8 && per_cta_threads(cluster * 2, vpt) >= 64)
+    cluster *= 2;
+  while (round_up(per_cta_threads(cluster, vpt), 32) > cta_max_threads(vpt) && vpt < 8)
+    vpt = next_supported_vpt(kCtaRows, vec, vpt + 1);
+  if (round_up(per_cta_threads(cluster, vpt), 32) > cta_max_threads(vpt)) {
+    p.kind = kTwoPass;
+    p.vpt = 4;
+    p.tpr = kTwoPassThreads;
+    p.cluster = 1;
+    return p;
+  }
+  p.kind = cluster > 1 ? kClusterRows : kCtaRows;
+  p.vpt = vpt;
+  p.cluster = cluster;
+  p.tpr = round_up(per_cta_threads(cluster, vpt), 32);
+  return p;
+}
+
+// Optional plan override for benchmarking and tuning (hprn_set_plan_override).
+std::string g_override;
+bool g_override_set = false;
+
+bool parse_plan(const std::string& s, Plan* p) {
+  char kind[16] = {0};
+  int vec, vpt, tpr, cluster, rpc;
+  if (sscanf(s.c_str(), "%15[a-z]:vec%d:vpt%d:tpr%d:cluster%d:rpc%d", kind, &vec, &vpt, &tpr,
+             &cluster, &rpc) != 6)
+    return false;
+  std::string k(kind);
+  if (k == "warp") p->kind = kWarpRows;
+  else if (k == "cta") p->kind = kCtaRows;
+  else if (k == "cluster") p->kind = kClusterRows;
+  else if (k == "twopass") p->kind = kTwoPass;
+  else return false;
+  p->vec = vec;
+  p->vpt = vpt;
+  p->tpr = tpr;
+  p->cluster = cluster;
+  p->rows_per_cta = rpc;
+  return true;
+}
+
+// Checks that `p` covers a row of `nvec` vectors within hardware limits.
+bool plan_valid(const Plan& p, int nvec, int max_vec, std::string* why) {
+  if (p.vec > max_vec || (p.vec != 32 && p.vec != 16 && p.vec != 8 && p.vec != 4 && p.vec != 2)) {
+    *why = "vector width not allowed by alignment / hidden size";
+    return false;
+  }
+  if (!vpt_supported(p.kind, p.vec, p.vpt)) {
+    *why = "vectors-per-thread value not compiled for this kernel";
+    return false;
+  }
+  switch (p.kind) {
+    case kWarpRows:
+      if (p.tpr != 32 || p.rows_per_cta < 1 || p.rows_per_cta > 8 || p.vpt * 32 < nvec) {
+        *why = "warp plan needs tpr 32, 1..8 rows per CTA and vpt*32 >= vectors per row";
+        return false;
+      }
+      return true;
+    case kCtaRows:
+    case kClusterRows: {
+      const int c = p.kind == kCtaRows ? 1 : p.cluster;
+      if (p.kind == kCtaRows && p.cluster != 1) {
+        *why = "cta plan needs cluster 1";
+        return false;
+      }
+      if (c < 1 || c > 8 || p.tpr < 32 || p.tpr > cta_max_threads(p.vpt) || p.tpr % 32) {
+        *why = "cluster must be 1..8 and tpr a multiple of 32 within the kernel's launch bound";
+        return false;
+      }
+      const int slice = (nvec + c - 1) / c;
+      if (static_cast<int64_t>(p.tpr) * p.vpt < slice) {
+        *why = "tpr * vpt does not cover the row slice";
+        return false;
+      }
+      return true;
+    }
+    default:
+      if (p.tpr < 32 || p.tpr > kTwoPassThreads || p.tpr % 32) {
+        *why = "twopass tpr must be a multiple of 32 in [32, 512]";
+        return false;
+      }
+      return true;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch: (dtype, vec, kind, vpt) -> kernel function pointer.
+
+using KernelFn = void (*)(RmsArgs);
+
+template <typename T, int VEC>
+KernelFn pick_warp(int vpt) {
+  switch (vpt) {
+    case 1: return rms_norm_warp_rows<T, VEC, 1>;
+    case 2: return rms_norm_warp_rows<T, VEC, 2>;
+    case 3: return rms_norm_warp_rows<T, VEC, 3>;
+    case 4: return rms_norm_warp_rows<T, VEC, 4>;
+  }
+  return nullptr;
+}
+
+template <typename T, int VEC, bool CL>
+KernelFn pick_cta(int vpt) {
+  if constexpr (VEC == 32) {
+    switch (vpt) {
+      case 3: return rms_norm_cta_rows<T, VEC, 3, CL>;
+      case 6: return rms_norm_cta_rows<T, VEC, 6, CL>;
+    }
+  }
+  switch (vpt) {
+    case 1: return rms_norm_cta_rows<T, VEC, 1, CL>;
+    case 2: return rms_norm_cta_rows<T, VEC, 2, CL>;
+    case 4: return rms_norm_cta_rows<T, VEC, 4, CL>;
+    case 8: return rms_norm_cta_rows<T, VEC, 8, CL>;
+  }
+  return nullptr;
+}
+
+template <typename T, int VEC>
+KernelFn pick_kind(const Plan& p) {
+  switch (p.kind) {
+    case kWarpRows: return pick_warp<T, VEC>(p.vpt);
+    case kCtaRows: return pick_cta<T, VEC, false>(p.vpt);
+    case kClusterRows: return pick_cta<T, VEC, true>(p.vpt);
+    default: return rms_norm_two_pass<T, VEC>;
+  }
+}
+
+template <typename T>
+KernelFn pick_vec(const Plan& p) {
+  switch (p.vec) {
+    case 32: return pick_kind<T, 32>(p);
+    case 16: return pick_kind<T, 16>(p);
+    case 8: return pick_kind<T, 8>(p);
+    case 4: return pick_kind<T, 4>(p);
+    default: return pick_kind<T, 2>(p);
+  }
+}
+
+KernelFn pick_kernel(int dtype, const Plan& p) {
+  return dtype == HPRN_DTYPE_BF16 ? pick_vec<__nv_bfloat16>(p) : pick_vec<__half>(p);
+}
+
+// Max CTAs per launch in grid.x (2^31 - 1), kept a multiple of 8 for clusters.
+constexpr int64_t kMaxGridX = 2147483640LL;
+
+struct Problem {
+  void* x;
+  const void* w;
+  void* r;
+  int64_t rows, hidden, xs, rs;
+  double eps;
+  int dtype;
+};
+
+int validate(const Problem& q) {
+  if (q.dtype != HPRN_DTYPE_BF16 && q.dtype != HPRN_DTYPE_FP16)
+    return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
+  if (q.rows < 0) return fail(HPRN_ERR_INVALID_ARGUMENT, "rows must be >= 0");
+  if (q.hidden < 1 || q.hidden > (static_cast<int64_t>(1) << 30))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "hidden_dim must be in [1, 2^30]");
+  if (q.rows == 0) return HPRN_OK;
+  if (!q.x || !q.w || !q.r) return fail(HPRN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned(q.x, 2) || !aligned(q.w, 2) || !aligned(q.r, 2))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor pointers must be 2-byte aligned");
+  if (q.rows > 1 && (q.xs < q.hidden || q.rs < q.hidden))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "row strides must be >= hidden_dim");
+  // input and residual must not share any element.
+  const int64_t xspan = (q.rows - 1) * q.xs + q.hidden;
+  const int64_t rspan = (q.rows - 1) * q.rs + q.hidden;
+  const char* xb = static_cast<const char*>(q.x);
+  const char* rb = static_cast<const char*>(q.r);
+  const bool spans_overlap = xb < rb + 2 * rspan && rb < xb + 2 * xspan;
+  if (spans_overlap) {
+    bool disjoint_rows = false;
+    const int64_t d = (rb - xb) / 2;
+    if (q.xs == q.rs && (rb - xb) % 2 == 0) {
+      const int64_t m = ((d % q.xs) + q.xs) % q.xs;
+      disjoint_rows = m >= q.hidden && q.xs - m >= q.hidden;
+    }
+    if (!disjoint_rows) return fail(HPRN_ERR_INVALID_ARGUMENT, "input and residual must not overlap");
+  }
+  return HPRN_OK;
+}
+
+int make_plan(const Problem& q, const DeviceInfo& dev, Plan* plan, RmsArgs* args) {
+  const int max_vec = choose_vec(q.hidden, q.rows, q.x, q.r, q.w, q.xs, q.rs);
+  const int nvec = static_cast<int>(q.hidden / (max_vec / 2));
+  Plan p = default_plan(q.rows, nvec, max_vec, dev);
+  if (g_override_set) {
+    Plan o;
+    std::string why;
+    if (!parse_plan(g_override, &o)) return fail(HPRN_ERR_INVALID_ARGUMENT, "unparsable plan override");
+    const int onvec = static_cast<int>(q.hidden / (o.vec / 2));
+    if (o.vec <= max_vec && q.hidden % (o.vec / 2) == 0 && plan_valid(o, onvec, max_vec, &why)) {
+      p = o;
+    } else if (o.vec <= max_vec && q.hidden % (o.vec / 2) == 0) {
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override rejected: " + why);
+    } else {
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override vector width not allowed here");
+    }
+  }
+  const int epv = p.vec / 2;
+  RmsArgs a;
+  a.x = static_cast<uint16_t*>(q.x);
+  a.w = static_cast<const uint16_t*>(q.w);
+  a.r = static_cast<uint16_t*>(q.r);
+  a.rows = q.rows;
+  a.x_stride = q.xs;
+  a.r_stride = q.rs;
+  a.nvec = static_cast<int>(q.hidden / epv);
+  a.slice_vecs = (a.nvec + p.cluster - 1) / p.cluster;
+  a.rows_per_cta = p.rows_per_cta;
+  a.eps = static_cast<float>(q.eps);
+  a.inv_hidden = 1.0f / static_cast<float>(q.hidden);
+  *plan = p;
+  *args = a;
+  return HPRN_OK;
+}
+
+int launch(const Plan& p, RmsArgs a, int dtype, cudaStream_t stream) {
+  KernelFn fn = pick_kernel(dtype, p);
+  if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
+  // Rows handled per CTA-group in grid.x; split very tall problems into launches.
+  const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;
+  const int64_t ctas_per_unit = p.kind == kClusterRows ? p.cluster : 1;
+  const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
+  int64_t done = 0;
+  while (done < a.rows) {
+    RmsArgs c = a;
+    const int64_t n = a.rows - done < max_rows ? a.rows - done : max_rows;
+    c.x = a.x + done * a.x_stride;
+    c.r = a.r + done * a.r_stride;
+    c.rows = n;
+    const int64_t units = (n + rows_per_unit - 1) / rows_per_unit;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(static_cast<unsigned>(units * ctas_per_unit), 1, 1);
+    cfg.blockDim = dim3(p.kind == kWarpRows ? 32 * p.rows_per_cta : p.tpr, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.numAttrs = 0;
+    if (p.kind == kClusterRows) {
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = p.cluster;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, c);
+    if (e != cudaSuccess)
+      return fail(HPRN_ERR_CUDA, std::string("rms_norm launch failed (") + plan_string(p) +
+                                     "): " + cudaGetErrorString(e));
+    done += n;
+  }
+  return HPRN_OK;
+}
+
+}  // namespace hprn
+
+extern "C" {
+
+int hprn_rms_norm(void* input, const void* weight, void* residual, int64_t rows, int64_t hidden,
+                  int64_t input_row_stride, int64_t residual_row_stride, double eps, int dtype,
+                  void* stream) {
+  using namespace hprn;
+  Problem q{input, weight, residual, rows, hidden, input_row_stride, residual_row_stride, eps, dtype};
+  int st = validate(q);
+  if (st != HPRN_OK) return st;
+  if (rows == 0) return ok();
+  const DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != HPRN_OK) return st;
+  Plan p;
+  RmsArgs a;
+  if ((st = make_plan(q, *dev, &p, &a)) != HPRN_OK) return st;
+  if ((st = launch(p, a, dtype, static_cast<cudaStream_t>(stream))) != HPRN_OK) return st;
+  return ok();
+}
+
+int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* input,
+                       const void* residual, int64_t input_row_stride,
+                       int64_t residual_row_stride, char* plan, int plan_len) {
+  using namespace hprn;
+  if (!plan || plan_len < 1) return fail(HPRN_ERR_INVALID_ARGUMENT, "plan buffer required");
+  if (dtype != HPRN_DTYPE_BF16 && dtype != HPRN_DTYPE_FP16)
+    return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
+  if (hidden < 1 || hidden > (static_cast<int64_t>(1) << 30))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "hidden_dim must be in [1, 2^30]");
+  // The weight's alignment is assumed to match the input's for planning.
+  Problem q{const_cast<void*>(input), input, const_cast<void*>(residual), rows < 1 ? 1 : rows,
+            hidden, input_row_stride, residual_row_stride, 1e-6, dtype};
+  int st;
+  const DeviceInfo* dev = nullptr;
+  DeviceInfo fake;
+  if (current_device(&dev) != HPRN_OK) {
+    // No usable device: plan for a 148-SM B200 so the heuristic can be inspected offline.
+    fake.sm_count = 148;
+    fake.cc_major = 10;
+    dev = &fake;
+  }
+  Plan p;
+  RmsArgs a;
+  if ((st = make_plan(q, *dev, &p, &a)) != HPRN_OK) return st;
+  snprintf(plan, plan_len, "%s", plan_string(p).c_str());
+  return ok();
+}
+
+int hprn_set_plan_override(const char* plan) {
+  using namespace hprn;
+  if (!plan || !*plan) {
+    g_override_set = false;
+    g_override.clear();
+    return ok();
+  }
+  Plan p;
+  if (!parse_plan(plan, &p)) return fail(HPRN_ERR_INVALID_ARGUMENT, "unparsable plan override");
+  g_override = plan;
+  g_override_set = true;
+  return ok();
+}
+
+}  // extern "C"

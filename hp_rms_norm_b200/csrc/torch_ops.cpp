@@ -1,0 +1,147 @@
+// torch.ops.hp_rms_norm.{rms_norm, relu}: the reference's operator surface,
+// implemented on top of the C ABI in include/hp_rms_norm_b200.h.
+//
+// Mirrors hp_rms_norm/csrc/hp_rms_norm.cpp:4-43 of the reference (the `_C`
+// module and the `hp_rms_norm` op namespace with the same op names and
+// argument order) and the argument checks of its host wrappers
+// (hp_rms_norm/csrc/cuda/hp_rms_norm.cu:12-24, activation_kernels.cu:11-16),
+// with the same check messages.  Added on top: dtype/device agreement between
+// the tensors, a device guard for the input's device (the reference launches
+// on whatever device is current), honest handling of row strides (the
+// reference assumes dense rows after view(-1, H)), mutation annotations in the
+// schemas and Meta kernels so the ops trace under torch.compile.
+#include <Python.h>
+
+#include <ATen/core/Tensor.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include "hp_rms_norm_b200.h"
+
+extern "C" {
+// An empty `_C` module: importing it loads this library, whose static
+// initialisers register the operators below.
+PyObject* PyInit__C(void) {
+  static struct PyModuleDef module_def = {PyModuleDef_HEAD_INIT, "_C", nullptr, -1, nullptr};
+  return PyModule_Create(&module_def);
+}
+}
+
+namespace {
+
+int dtype_code(const at::Tensor& t) {
+  if (t.scalar_type() == at::kBFloat16) return HPRN_DTYPE_BF16;
+  if (t.scalar_type() == at::kHalf) return HPRN_DTYPE_FP16;
+  TORCH_CHECK(false, "dtype must be kFloat16 or kBFloat16");
+}
+
+// Rows of a [..., hidden] tensor whose last dim is contiguous: the number of
+// rows and the stride between consecutive rows, or an error when the leading
+// dims cannot be walked with one stride (the case where the reference's
+// view(-1, hidden) throws).
+void rows_of(const at::Tensor& t, const char* name, int64_t* rows, int64_t* stride) {
+  const int64_t hidden = t.size(-1);
+  int64_t n = 1;
+  for (int64_t i = 0; i + 1 < t.dim(); ++i) n *= t.size(i);
+  *rows = n;
+  *stride = hidden;
+  if (n <= 1) return;
+  int64_t expect = -1;  // stride the next-outer non-trivial dim must have
+  int64_t row_stride = -1;
+  for (int64_t i = t.dim() - 2; i >= 0; --i) {
+    if (t.size(i) == 1) continue;
+    if (row_stride < 0) {
+      row_stride = t.stride(i);
+      expect = t.stride(i) * t.size(i);
+    } else {
+      TORCH_CHECK(t.stride(i) == expect, name,
+                  " must be viewable as (-1, hidden_dim): its leading dimensions are not "
+                  "collapsible into rows of one stride");
+      expect = t.stride(i) * t.size(i);
+    }
+  }
+  *stride = row_stride;
+}
+
+void check_status(int status) {
+  TORCH_CHECK(status == HPRN_OK, hprn_status_string(status), ": ", hprn_last_error());
+}
+
+void rms_norm(at::Tensor& input, const at::Tensor& weight, at::Tensor& residual, double eps) {
+  // hp_rms_norm/csrc/cuda/hp_rms_norm.cu:12-24
+  TORCH_CHECK(input.dim() >= 2, "input.dim() >= 2");
+  TORCH_CHECK(input.dim() == residual.dim(), "input.dim() == residual.dim()");
+  for (int64_t i = 0; i < input.dim(); ++i) {
+    TORCH_CHECK(input.size(i) == residual.size(i), "input.size(i) == residual.size(i)");
+  }
+  TORCH_CHECK(weight.dim() == 1, "weight.dim() == 1");
+  const int64_t hidden = weight.size(0);
+  TORCH_CHECK(input.size(-1) == hidden, "input.size(-1) == hidden_dim");
+  TORCH_CHECK(input.stride(-1) == 1, "input.stride(-1) == 1");
+  TORCH_CHECK(residual.stride(-1) == 1, "residual.stride(-1) == 1");
+  // Added checks.
+  TORCH_CHECK(input.is_cuda() && weight.is_cuda() && residual.is_cuda(),
+              "input, weight and residual must be CUDA tensors");
+  TORCH_CHECK(weight.device() == input.device() && residual.device() == input.device(),
+              "input, weight and residual must be on the same device");
+  TORCH_CHECK(weight.scalar_type() == input.scalar_type() &&
+                  residual.scalar_type() == input.scalar_type(),
+              "input, weight and residual must have the same dtype");
+  TORCH_CHECK(hidden <= 1 || weight.stride(0) == 1, "weight must be contiguous");
+  const int dtype = dtype_code(input);
+  int64_t rows = 0, xs = 0, rrows = 0, rs = 0;
+  rows_of(input, "input", &rows, &xs);
+  rows_of(residual, "residual", &rrows, &rs);
+  if (rows == 0 || hidden == 0) return;
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_rms_norm(input.data_ptr(), weight.data_ptr(), residual.data_ptr(), rows, hidden,
+                             xs, rs, eps, dtype, stream));
+}
+
+void relu(at::Tensor& out, const at::Tensor& input) {
+  // hp_rms_norm/csrc/cuda/activation_kernels.cu:11-16
+  TORCH_CHECK(input.dim() >= 2, "input.dim() >= 2");
+  TORCH_CHECK(input.dim() == out.dim(), "input.size(i) == out.size(i)");
+  for (int64_t i = 0; i < input.dim(); ++i) {
+    TORCH_CHECK(input.size(i) == out.size(i), "input.size(i) == out.size(i)");
+  }
+  // Added checks.
+  TORCH_CHECK(input.is_cuda() && out.is_cuda(), "out and input must be CUDA tensors");
+  TORCH_CHECK(out.device() == input.device(), "out and input must be on the same device");
+  TORCH_CHECK(out.scalar_type() == input.scalar_type(), "out and input must have the same dtype");
+  const int dtype = dtype_code(input);
+  const int64_t hidden = input.size(-1);
+  if (input.numel() == 0) return;
+  TORCH_CHECK(hidden == 1 || input.stride(-1) == 1, "input.stride(-1) == 1");
+  TORCH_CHECK(hidden == 1 || out.stride(-1) == 1, "out.stride(-1) == 1");
+  int64_t rows = 0, is = 0, orows = 0, os = 0;
+  rows_of(input, "input", &rows, &is);
+  rows_of(out, "out", &orows, &os);
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_relu(out.data_ptr(), input.data_ptr(), rows, hidden, os, is, dtype, stream));
+}
+
+// Shape-only kernels for tracing (torch.compile / FakeTensor): the ops return
+// nothing and only mutate their annotated arguments.
+void rms_norm_meta(at::Tensor&, const at::Tensor&, at::Tensor&, double) {}
+void relu_meta(at::Tensor&, const at::Tensor&) {}
+
+}  // namespace
+
+TORCH_LIBRARY(hp_rms_norm, m) {
+  m.def("rms_norm(Tensor(a!) input, Tensor weight, Tensor(b!) residual, float eps) -> ()");
+  m.def("relu(Tensor(a!) out, Tensor input) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(hp_rms_norm, CUDA, m) {
+  m.impl("rms_norm", &rms_norm);
+  m.impl("relu", &relu);
+}
+
+TORCH_LIBRARY_IMPL(hp_rms_norm, Meta, m) {
+  m.impl("rms_norm", &rms_norm_meta);
+  m.impl("relu", &relu_meta);
+}

@@ -1,0 +1,290 @@
+// Vector memory access and 16-bit float packing helpers for sm_100a.
+//
+// A "vector" is VEC bytes of one row: 32 (ld/st.global.v8.b32, the Blackwell
+// 256-bit access), 16, 8, 4 or 2 bytes.  Elements are 16-bit (bf16 or fp16)
+// and travel as raw bit patterns; arithmetic is fp32.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace hprn {
+
+template <int VEC>
+struct Vec {
+  static constexpr int kWords = VEC / 4;  // 32-bit words
+  static constexpr int kElems = VEC / 2;  // 16-bit elements
+  uint32_t w[kWords];
+};
+
+template <>
+struct Vec<2> {
+  static constexpr int kWords = 0;
+  static constexpr int kElems = 1;
+  uint16_t h;
+};
+
+// ---------------------------------------------------------------------------
+// L2 cache policies (createpolicy): streamed rows are read once, so they are
+// marked evict_first; the weight row is re-read by every row and is kept with
+// evict_last.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// Streaming loads: bypass L1 allocation, L2 evict_first.
+template <int VEC>
+__device__ __forceinline__ Vec<VEC> ld_stream(const void* p, uint64_t pol);
+
+template <>
+__device__ __forceinline__ Vec<32> ld_stream<32>(const void* p, uint64_t pol) {
+  Vec<32> v;
+  asm volatile(
+      "ld.global.L1::no_allocate.L2::cache_hint.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+      : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+        "=r"(v.w[6]), "=r"(v.w[7])
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<16> ld_stream<16>(const void* p, uint64_t pol) {
+  Vec<16> v;
+  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v4.b32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<8> ld_stream<8>(const void* p, uint64_t pol) {
+  Vec<8> v;
+  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.v2.b32 {%0,%1}, [%2], %3;"
+               : "=r"(v.w[0]), "=r"(v.w[1])
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<4> ld_stream<4>(const void* p, uint64_t pol) {
+  Vec<4> v;
+  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.b32 %0, [%1], %2;"
+               : "=r"(v.w[0])
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<2> ld_stream<2>(const void* p, uint64_t pol) {
+  Vec<2> v;
+  asm volatile("ld.global.L1::no_allocate.L2::cache_hint.b16 %0, [%1], %2;"
+               : "=h"(v.h)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Weight loads: read-only path, kept in L1 and (evict_last) in L2.
+template <int VEC>
+__device__ __forceinline__ Vec<VEC> ld_weight(const void* p, uint64_t pol);
+
+template <>
+__device__ __forceinline__ Vec<32> ld_weight<32>(const void* p, uint64_t pol) {
+  Vec<32> v;
+  asm volatile(
+      "ld.global.nc.L1::evict_last.L2::cache_hint.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+      : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+        "=r"(v.w[6]), "=r"(v.w[7])
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<16> ld_weight<16>(const void* p, uint64_t pol) {
+  Vec<16> v;
+  asm volatile("ld.global.nc.L1::evict_last.L2::cache_hint.v4.b32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<8> ld_weight<8>(const void* p, uint64_t pol) {
+  Vec<8> v;
+  asm volatile("ld.global.nc.L1::evict_last.L2::cache_hint.v2.b32 {%0,%1}, [%2], %3;"
+               : "=r"(v.w[0]), "=r"(v.w[1])
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<4> ld_weight<4>(const void* p, uint64_t pol) {
+  Vec<4> v;
+  asm volatile("ld.global.nc.L1::evict_last.L2::cache_hint.b32 %0, [%1], %2;"
+               : "=r"(v.w[0])
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<2> ld_weight<2>(const void* p, uint64_t pol) {
+  Vec<2> v;
+  asm volatile("ld.global.nc.L1::evict_last.L2::cache_hint.b16 %0, [%1], %2;"
+               : "=h"(v.h)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Plain loads that must observe this kernel's own earlier stores (the
+// two-pass kernel re-reads the residual it just wrote): L1 is bypassed with
+// .cg so the line comes from L2.
+template <int VEC>
+__device__ __forceinline__ Vec<VEC> ld_l2(const void* p);
+
+template <>
+__device__ __forceinline__ Vec<32> ld_l2<32>(const void* p) {
+  Vec<32> v;
+  asm volatile("ld.global.cg.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]),
+                 "=r"(v.w[5]), "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<16> ld_l2<16>(const void* p) {
+  Vec<16> v;
+  asm volatile("ld.global.cg.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<8> ld_l2<8>(const void* p) {
+  Vec<8> v;
+  asm volatile("ld.global.cg.v2.b32 {%0,%1}, [%2];" : "=r"(v.w[0]), "=r"(v.w[1]) : "l"(p) : "memory");
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<4> ld_l2<4>(const void* p) {
+  Vec<4> v;
+  asm volatile("ld.global.cg.b32 %0, [%1];" : "=r"(v.w[0]) : "l"(p) : "memory");
+  return v;
+}
+
+template <>
+__device__ __forceinline__ Vec<2> ld_l2<2>(const void* p) {
+  Vec<2> v;
+  asm volatile("ld.global.cg.b16 %0, [%1];" : "=h"(v.h) : "l"(p) : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Stores.
+template <int VEC>
+__device__ __forceinline__ void st_global(void* p, const Vec<VEC>& v);
+
+template <>
+__device__ __forceinline__ void st_global<32>(void* p, const Vec<32>& v) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]),
+               "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]),
+               "r"(v.w[7])
+               : "memory");
+}
+
+template <>
+__device__ __forceinline__ void st_global<16>(void* p, const Vec<16>& v) {
+  asm volatile("st.global.v4.b32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+               "r"(v.w[2]), "r"(v.w[3])
+               : "memory");
+}
+
+template <>
+__device__ __forceinline__ void st_global<8>(void* p, const Vec<8>& v) {
+  asm volatile("st.global.v2.b32 [%0], {%1,%2};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]) : "memory");
+}
+
+template <>
+__device__ __forceinline__ void st_global<4>(void* p, const Vec<4>& v) {
+  asm volatile("st.global.b32 [%0], %1;" ::"l"(p), "r"(v.w[0]) : "memory");
+}
+
+template <>
+__device__ __forceinline__ void st_global<2>(void* p, const Vec<2>& v) {
+  asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(v.h) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// 16-bit float <-> fp32.  T is __nv_bfloat16 or __half.  Pairs use the packed
+// conversions (cvt.rn.bf16x2.f32 / cvt.rn.f16x2.f32), round to nearest even.
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  return __half22float2(h);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T>
+__device__ __forceinline__ float unpack1(uint16_t h);
+
+template <>
+__device__ __forceinline__ float unpack1<__nv_bfloat16>(uint16_t h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+
+template <>
+__device__ __forceinline__ float unpack1<__half>(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+template <typename T>
+__device__ __forceinline__ uint16_t pack1(float f);
+
+template <>
+__device__ __forceinline__ uint16_t pack1<__nv_bfloat16>(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+template <>
+__device__ __forceinline__ uint16_t pack1<__half>(float f) {
+  return __half_as_ushort(__float2half_rn(f));
+}
+
+}  // namespace hprn

@@ -1,0 +1,125 @@
+/*
+ * hp_rms_norm_b200: C ABI of the B200-native (sm_100a) fused residual-add +
+ * RMSNorm and ReLU kernels.
+ *
+ * Everything here is plain C: device pointers, element counts and strides, a
+ * dtype code and a CUDA stream handle passed as void*.  No torch types cross
+ * this boundary.  The torch-extension binding (torch.ops.hp_rms_norm.*) and
+ * any cgo / JNI / ctypes caller bind these same symbols.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are device pointers on the CURRENT CUDA device of
+ *     the calling thread (cudaSetDevice before calling).
+ *   - Work is enqueued asynchronously on `stream` (a cudaStream_t; NULL means
+ *     the legacy default stream).  Nothing synchronises; nothing allocates.
+ *   - Return value: HPRN_OK (0) or a negative hprn_status code; on error no
+ *     kernel was launched (except HPRN_ERR_CUDA, which reports a failed
+ *     launch) and hprn_last_error() returns a message for this thread.
+ *   - Strides are in ELEMENTS, between consecutive rows; elements within a
+ *     row are contiguous.
+ */
+#ifndef HP_RMS_NORM_B200_H_
+#define HP_RMS_NORM_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HPRN_VERSION 10000 /* 1.0.0 */
+
+#if defined(__GNUC__)
+#define HPRN_API __attribute__((visibility("default")))
+#else
+#define HPRN_API
+#endif
+
+typedef enum hprn_dtype {
+  HPRN_DTYPE_BF16 = 0, /* torch.bfloat16 / __nv_bfloat16 */
+  HPRN_DTYPE_FP16 = 1  /* torch.float16  / __half        */
+} hprn_dtype;
+
+typedef enum hprn_status {
+  HPRN_OK = 0,
+  HPRN_ERR_INVALID_ARGUMENT = -1, /* bad size, stride, null pointer, overlap */
+  HPRN_ERR_UNSUPPORTED_DTYPE = -2,
+  HPRN_ERR_UNSUPPORTED_DEVICE = -3, /* not an sm_100 (B200-class) device */
+  HPRN_ERR_CUDA = -4                /* a CUDA runtime call or launch failed */
+} hprn_status;
+
+/*
+ * Fused residual add + RMSNorm, in place:
+ *
+ *   residual[i, :] <- round_T(f32(input[i, :]) + f32(residual[i, :]))
+ *   input[i, :]    <- round_T(f32(residual[i, :]) * f32(weight[:]) * inv_i)
+ *   inv_i           = rsqrt(eps + sum_j s_ij^2 / hidden),  s_ij the fp32 sum before rounding
+ *
+ * for rows i in [0, rows).  input and residual must not overlap.
+ *
+ * Replaces the reference's torch-op implementation
+ *   void rms_norm(Tensor& input, const Tensor& weight, Tensor& residual, double eps)
+ *     hp_rms_norm/csrc/cuda/hp_rms_norm.cu:7-50
+ * and its launcher hp_rms_norm::launch_rms_norm<T>
+ *     hp_rms_norm/csrc/cuda/hp_rms_norm.cuh:562-618
+ * (there `rows` is the reference's `tokens` and both strides equal hidden).
+ * Unlike the reference it accepts any hidden >= 1, any 2-byte-aligned pointers
+ * and independent row strides; the widest vector width the pointers, strides
+ * and hidden size allow is chosen per call.
+ */
+HPRN_API int hprn_rms_norm(void* input, const void* weight, void* residual, int64_t rows,
+                           int64_t hidden, int64_t input_row_stride, int64_t residual_row_stride,
+                           double eps, int dtype, void* stream);
+
+/*
+ * Elementwise ReLU, out-of-place: out[i, :] = input[i, :] < 0 ? +0 : input[i, :]
+ * (torch.relu: -0.0 and NaN pass through with their bits unchanged, -inf -> +0).
+ * out and input may be the same pointer (in place) but must not otherwise overlap.
+ *
+ * Replaces the reference's
+ *   void relu(Tensor& out, const Tensor& input)
+ *     hp_rms_norm/csrc/cuda/activation_kernels.cu:7-39
+ * and hp_rms_norm::launch_relu<T> hp_rms_norm/csrc/cuda/activation_kernels.cuh:122-145.
+ * (The reference kernel copies input to out without applying max(x, 0) and
+ * drops the row tail when hidden * 2 is not a multiple of 256; this entry point
+ * applies ReLU to every element.)
+ */
+HPRN_API int hprn_relu(void* out, const void* input, int64_t rows, int64_t hidden,
+                       int64_t out_row_stride, int64_t input_row_stride, int dtype, void* stream);
+
+/* Message for the last non-OK status returned on this thread ("" if none). */
+HPRN_API const char* hprn_last_error(void);
+
+/* Static name of a status code. */
+HPRN_API const char* hprn_status_string(int status);
+
+/* HPRN_VERSION of the loaded library. */
+HPRN_API int hprn_version(void);
+
+/*
+ * Launch-plan introspection (for tests and benchmarks): writes the plan that
+ * hprn_rms_norm would use for this problem on the current device into
+ * `plan` as a NUL-terminated string "<kind>:vec<V>:vpt<P>:tpr<T>:cluster<C>:rpc<R>"
+ * (kind warp | cta | cluster | twopass; V bytes per vector access; P vectors
+ * per thread; T threads per CTA; C CTAs per row; R rows per CTA) and returns
+ * HPRN_OK.  Performs no launch.  Null input/residual pointers plan for
+ * 256-byte-aligned tensors; without a usable device it plans for a 148-SM B200.
+ */
+HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* input,
+                                const void* residual, int64_t input_row_stride,
+                                int64_t residual_row_stride, char* plan, int plan_len);
+
+/*
+ * Tuning hook: force the launch plan of every later hprn_rms_norm call in this
+ * process (same string format as hprn_rms_norm_plan; NULL or "" restores the
+ * built-in heuristic).  A forced plan that does not fit a call makes that call
+ * fail with HPRN_ERR_INVALID_ARGUMENT.  Process-global, not thread-safe: meant
+ * for benchmarks and launch-shape sweeps, not for production callers.
+ */
+HPRN_API int hprn_set_plan_override(const char* plan);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HP_RMS_NORM_B200_H_ */

@@ -1,0 +1,152 @@
+/*
+ * CPU oracle for the fused residual-add + RMSNorm path and the companion ReLU.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker that the CUDA path is
+ * compared against; it is never linked into, loaded by or called from the
+ * product library.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline leg may use it.
+ *
+ * It restates, element by element and in plain C, the arithmetic of the
+ * reference implementation (HydraQYH/hp_rms_norm):
+ *
+ *   hp_rms_norm/csrc/cuda/hp_rms_norm.cuh:186-193  s   = f32(x) + f32(r)   (fp32 add)
+ *                                                  r'  = round_T(s)         (RN-even)
+ *                                                  ss += s * s              (unrounded s)
+ *   hp_rms_norm/csrc/cuda/hp_rms_norm.cuh:231      inv = rsqrt(eps + ss / H)
+ *   hp_rms_norm/csrc/cuda/hp_rms_norm.cuh:104-110  y   = round_T(f32(r') * f32(w) * inv)
+ *
+ * and the reference test's eager formula (test/test_hp_rms_norm.py:6-19:
+ * inp_res = inp + res in T, then torch.rms_norm on the rounded sum), which
+ * differs only in squaring the rounded residual: select it with
+ * ss_mode = ORACLE_SS_ROUNDED.
+ *
+ * The sum of squares is accumulated in double and the inverse RMS is computed
+ * in double then rounded once to float, so the oracle is at least as accurate
+ * as any fp32-accumulating kernel.  The output product is then formed in float,
+ * left to right, exactly as hp_rms_norm.cuh:108-109 writes it.
+ *
+ * ReLU follows torch.relu bit for bit: x < 0 ? +0 : x, so -0.0 and NaN pass
+ * through unchanged and -inf becomes +0.  (The reference's "relu" kernel,
+ * hp_rms_norm/csrc/cuda/activation_kernels.cuh:99-119, is a plain copy; the
+ * product follows torch.relu instead.)
+ *
+ * Storage is raw 16-bit patterns (uint16_t) for both bf16 and fp16.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORACLE_BF16 0
+#define ORACLE_FP16 1
+#define ORACLE_SS_UNROUNDED 0 /* the CUDA kernel (hp_rms_norm.cuh:190-193) */
+#define ORACLE_SS_ROUNDED 1   /* the test's eager formula (test_hp_rms_norm.py:13-19) */
+
+/* ---- bf16 ------------------------------------------------------------- */
+
+static inline float bf16_to_f32(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+/* Round to nearest, ties to even.  NaN maps to the canonical quiet NaN. */
+static inline uint16_t f32_to_bf16_rn(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)(((u >> 16) & 0x8000u) | 0x7fc0u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+/* ---- fp16 (IEEE binary16 through the compiler's _Float16, RN-even) ----- */
+
+static inline float f16_to_f32(uint16_t b) {
+  _Float16 h;
+  memcpy(&h, &b, 2);
+  return (float)h;
+}
+
+static inline uint16_t f32_to_f16_rn(float f) {
+  _Float16 h = (_Float16)f;
+  uint16_t b;
+  memcpy(&b, &h, 2);
+  return b;
+}
+
+static inline float to_f32(int dtype, uint16_t b) {
+  return dtype == ORACLE_BF16 ? bf16_to_f32(b) : f16_to_f32(b);
+}
+
+static inline uint16_t from_f32(int dtype, float f) {
+  return dtype == ORACLE_BF16 ? f32_to_bf16_rn(f) : f32_to_f16_rn(f);
+}
+
+/* Exported conversion helpers, so the Python side can pin them against numpy. */
+void oracle_to_f32(int dtype, const uint16_t* in, float* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = to_f32(dtype, in[i]);
+}
+
+void oracle_from_f32(int dtype, const float* in, uint16_t* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = from_f32(dtype, in[i]);
+}
+
+/* One row: the whole per-row computation of hp_rms_norm.cuh:149-252. */
+static void fused_add_rms_norm_row(int dtype, uint16_t* x, const uint16_t* w, uint16_t* r,
+                                   int64_t hidden, double eps, int ss_mode) {
+  double ss = 0.0;
+  for (int64_t j = 0; j < hidden; ++j) {
+    float s = to_f32(dtype, x[j]) + to_f32(dtype, r[j]);
+    uint16_t rr = from_f32(dtype, s);
+    r[j] = rr;
+    double v = (ss_mode == ORACLE_SS_ROUNDED) ? (double)to_f32(dtype, rr) : (double)s;
+    ss += v * v;
+  }
+  float inv = (float)(1.0 / sqrt(ss / (double)hidden + eps));
+  for (int64_t j = 0; j < hidden; ++j) {
+    float y = to_f32(dtype, r[j]) * to_f32(dtype, w[j]) * inv;
+    x[j] = from_f32(dtype, y);
+  }
+}
+
+/*
+ * In place, like rms_norm(input, weight, residual, eps)
+ * (hp_rms_norm/csrc/cuda/hp_rms_norm.cu:7-50): residual <- input + residual,
+ * input <- RMSNorm(residual) * weight.  Row i of input starts at
+ * input + i * in_stride, row i of residual at residual + i * res_stride
+ * (both in elements).
+ */
+void oracle_fused_add_rms_norm(int dtype, uint16_t* input, const uint16_t* weight,
+                               uint16_t* residual, int64_t rows, int64_t hidden,
+                               int64_t in_stride, int64_t res_stride, double eps,
+                               int ss_mode) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    fused_add_rms_norm_row(dtype, input + i * in_stride, weight, residual + i * res_stride,
+                           hidden, eps, ss_mode);
+  }
+}
+
+/* torch.relu on raw 16-bit patterns: negative finite values and -inf become +0. */
+void oracle_relu(int dtype, uint16_t* out, const uint16_t* in, int64_t n) {
+  const uint16_t inf_bits = dtype == ORACLE_BF16 ? 0x7f80u : 0x7c00u;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    uint16_t b = in[i];
+    uint16_t mag = (uint16_t)(b & 0x7fffu);
+    int negative = (b & 0x8000u) && mag != 0 && mag <= inf_bits; /* not -0, not NaN */
+    out[i] = negative ? (uint16_t)0 : b;
+  }
+}
+
+int oracle_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

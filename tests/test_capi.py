@@ -1,0 +1,124 @@
+"""The C-ABI library on CPU: it loads, exports what the header declares, plans,
+and rejects bad arguments before touching a device (no kernel is launched by
+any test here: every call below fails validation first)."""
+import os
+import re
+
+import pytest
+
+from hp_rms_norm_b200 import capi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    syms = set()
+    for name in os.listdir(os.path.join(ROOT, "include")):
+        if name.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", name)).read()
+            syms |= set(re.findall(r"HPRN_API\s+[\w\s\*]*?\b(hprn_\w+)\s*\(", text))
+    return syms
+
+
+def test_header_declares_expected_symbols():
+    assert header_symbols() == set(capi.EXPORTED)
+
+
+def test_library_exports_every_header_symbol():
+    lib = capi.load()
+    for sym in header_symbols():
+        assert hasattr(lib, sym), sym
+
+
+def test_version_and_status_strings():
+    assert capi.version() == 10000
+    lib = capi.load()
+    assert lib.hprn_status_string(0) == b"HPRN_OK"
+    assert lib.hprn_status_string(-1) == b"HPRN_ERR_INVALID_ARGUMENT"
+    assert lib.hprn_status_string(-4) == b"HPRN_ERR_CUDA"
+    assert lib.hprn_status_string(99) == b"HPRN_ERR_UNKNOWN"
+
+
+@pytest.mark.parametrize("rows,hidden,kind", [
+    (4096, 1024, "warp"), (4096, 2048, "warp"), (4096, 4096, "cta"), (4096, 8192, "cta"),
+    (4096, 16384, "cluster"), (4096, 32768, "cluster"), (1, 8192, "cluster"),
+    (3, 1 << 22, "twopass"),
+])
+def test_plan_kinds(rows, hidden, kind):
+    p = capi.plan(rows, hidden)
+    assert p.startswith(kind + ":"), p
+    assert ":vec32:" in p
+
+
+def test_plan_vector_width_follows_alignment_and_hidden():
+    assert ":vec32:" in capi.plan(8, 4096, input_ptr=256, residual_ptr=1 << 20)
+    assert ":vec16:" in capi.plan(8, 4096, input_ptr=256 + 16, residual_ptr=1 << 20)
+    assert ":vec8:" in capi.plan(8, 4100)
+    assert ":vec4:" in capi.plan(8, 4098)
+    assert ":vec2:" in capi.plan(8, 4097)
+    assert ":vec16:" in capi.plan(8, 4096, input_row_stride=4104)
+
+
+def test_plan_covers_every_row_length():
+    """Every plan's threads x vectors x CTAs covers the row (no element dropped)."""
+    for hidden in list(range(1, 300)) + [1000, 4095, 5120, 13312, 20480, 65536, 262144, 1 << 20]:
+        p = capi.plan(4, hidden)
+        f = dict(re.findall(r"([a-z]+)(\d+)", p))
+        vec, vpt, tpr, cl = (int(f[k]) for k in ("vec", "vpt", "tpr", "cluster"))
+        nvec = hidden // (vec // 2)
+        assert hidden % (vec // 2) == 0, (hidden, p)
+        if p.startswith("warp"):
+            assert vpt * 32 >= nvec, (hidden, p)
+        elif not p.startswith("twopass"):
+            assert tpr * vpt * cl >= nvec, (hidden, p)
+
+
+def expect_error(status_fn, status, fragment):
+    with pytest.raises(capi.HprnError) as e:
+        status_fn()
+    assert e.value.status == status
+    assert fragment in str(e.value)
+
+
+def test_rms_norm_argument_errors_before_any_launch():
+    F = 1 << 20  # fake device addresses: every call below must be rejected by validation
+    bf = capi.DTYPE_BF16
+    expect_error(lambda: capi.rms_norm(F, F, F, 4, 8, 8, 8, 1e-6, 7), capi.ERR_UNSUPPORTED_DTYPE,
+                 "dtype must be kFloat16 or kBFloat16")
+    expect_error(lambda: capi.rms_norm(F, F, 2 * F, -1, 8, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "rows")
+    expect_error(lambda: capi.rms_norm(F, F, 2 * F, 4, 0, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "hidden_dim")
+    expect_error(lambda: capi.rms_norm(0, F, 2 * F, 4, 8, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "null")
+    expect_error(lambda: capi.rms_norm(F + 1, F, 2 * F, 4, 8, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "aligned")
+    expect_error(lambda: capi.rms_norm(F, F, 2 * F, 4, 8, 4, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "strides")
+    # residual starts inside input's rows
+    expect_error(lambda: capi.rms_norm(F, F, F + 8, 4, 8, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "overlap")
+    expect_error(lambda: capi.rms_norm(F, F, F, 4, 8, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "overlap")
+
+
+def test_rms_norm_zero_rows_is_a_no_op():
+    capi.rms_norm(0, 0, 0, 0, 4096, 4096, 4096, 1e-6, capi.DTYPE_BF16)
+
+
+def test_relu_argument_errors_before_any_launch():
+    F = 1 << 20
+    bf = capi.DTYPE_BF16
+    expect_error(lambda: capi.relu(F, 2 * F, 4, 8, 8, 8, 5), capi.ERR_UNSUPPORTED_DTYPE, "dtype")
+    expect_error(lambda: capi.relu(F, 2 * F, -1, 8, 8, 8, bf), capi.ERR_INVALID_ARGUMENT, ">= 0")
+    expect_error(lambda: capi.relu(0, 2 * F, 4, 8, 8, 8, bf), capi.ERR_INVALID_ARGUMENT, "null")
+    expect_error(lambda: capi.relu(F + 2, F, 4, 8, 8, 8, bf), capi.ERR_INVALID_ARGUMENT, "overlap")
+    expect_error(lambda: capi.relu(F, 2 * F, 4, 8, 4, 8, bf), capi.ERR_INVALID_ARGUMENT, "strides")
+    capi.relu(0, 0, 0, 8, 8, 8, bf)  # empty: no-op
+
+
+def test_plan_override_parsing():
+    expect_error(lambda: capi.set_plan_override("nonsense"), capi.ERR_INVALID_ARGUMENT, "unparsable")
+    capi.set_plan_override("cta:vec32:vpt2:tpr128:cluster1:rpc1")
+    capi.set_plan_override(None)
+    assert capi.plan(4096, 4096).startswith("cta:")
