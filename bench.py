@@ -69,11 +69,15 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["sweep", "config0", "shard", "decode", "relu"],
                     default="sweep")
+    ap.add_argument("--hidden", default=None,
+                    help="comma-separated hidden sizes: restrict the sweep (e.g. for ncu captures)")
+    ap.add_argument("--rows", type=int, default=BATCH, help="batch rows of the sweep/config0")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU work budget of the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--out", default=None, help="also write the JSON line to this file")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -230,6 +234,36 @@ def make_rows(rows, hidden, dtype, device, seed):
     return x, w, r
 
 
+def per_shape_us(torch, launch, i, rows, h, dev, min_bytes=600e6, reps=3):
+    """Cold per-launch time of shape i: graph of back-to-back launches over
+    rotating buffer sets."""
+    set_bytes = rows * h * ELEM * 2
+    nsets = min(256, max(2, int(-(-min_bytes // set_bytes))))  # tiny shapes: <= 256 sets
+    L = max(16, nsets)
+    xs = [torch.randn(rows, h, device=dev).to(torch.bfloat16) for _ in range(nsets)]
+    rs = [torch.randn(rows, h, device=dev).to(torch.bfloat16) for _ in range(nsets)]
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        launch(i, s.cuda_stream, xs[0], rs[0])
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for k in range(L):
+            launch(i, s.cuda_stream, xs[k % nsets], rs[k % nsets])
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g, xs, rs
+    torch.cuda.empty_cache()
+    return e0.elapsed_time(e1) * 1e3 / (reps * L)
+
+
 def cpu_eager_sample(shapes, seconds: float):
     """Times the reference formula on the host cores over a bounded sample.
 
@@ -278,12 +312,16 @@ def run_ours(args, dist):
     # ---- problem list for one step --------------------------------------
     scaling = "weak"
     if args.workload == "sweep":
-        shapes = [(BATCH, h) for h in SWEEP]
-        workload = ("config1: fused add+RMSNorm hidden sweep 1024..16384 step 1024 + 20480, "
-                    "24576, 28672, 32768 at batch 4096 bf16 (20 launches per step)")
+        hs = [int(h) for h in args.hidden.split(",")] if args.hidden else SWEEP
+        shapes = [(args.rows, h) for h in hs]
+        if hs == SWEEP and args.rows == BATCH:
+            workload = ("config1: fused add+RMSNorm hidden sweep 1024..16384 step 1024 + 20480, "
+                        "24576, 28672, 32768 at batch 4096 bf16 (20 launches per step)")
+        else:
+            workload = f"config1 subset: batch {args.rows} bf16, hidden {hs}"
     elif args.workload == "config0":
-        shapes = [(BATCH, 4096)]
-        workload = "config0: fused add+RMSNorm 4096 x 4096 bf16"
+        shapes = [(args.rows, 4096)]
+        workload = f"config0: fused add+RMSNorm {args.rows} x 4096 bf16"
     elif args.workload == "shard":
         scaling = "strong"
         shapes = []
@@ -307,14 +345,34 @@ def run_ours(args, dist):
     step_bytes = sum(alg_bytes(rows, h) for rows, h in shapes)
     eps = 1e-6
 
+    # Consecutive launches of the same kernel template form a group; the timed
+    # loop records one event per group boundary (a handful per step), so the
+    # dominant kernel's launch time is measured inside the timed region without
+    # an event pair around every launch.
+    kern_of = [p.split(":tpr")[0] for p in plans]
+    groups = []  # (kernel, [shape indices])
+    for i, k in enumerate(kern_of):
+        if groups and groups[-1][0] == k:
+            groups[-1][1].append(i)
+        else:
+            groups.append((k, [i]))
+
+    def launch(i, stream_handle, x=None, r=None):
+        rows, h = shapes[i]
+        bx, bw, br = bufs[i]
+        x = bx if x is None else x
+        r = br if r is None else r
+        capi.rms_norm(x.data_ptr(), bw.data_ptr(), r.data_ptr(), rows, h, h, h, eps,
+                      capi.DTYPE_BF16, stream_handle)
+
     def one_step(evs=None):
-        for i, ((rows, h), (x, w, r)) in enumerate(zip(shapes, bufs)):
+        for g, (_, idx) in enumerate(groups):
             if evs is not None:
-                evs[i][0].record(stream)
-            capi.rms_norm(x.data_ptr(), w.data_ptr(), r.data_ptr(), rows, h, h, h, eps,
-                          capi.DTYPE_BF16, sh)
-            if evs is not None:
-                evs[i][1].record(stream)
+                evs[g].record(stream)
+            for i in idx:
+                launch(i, sh)
+        if evs is not None:
+            evs[len(groups)].record(stream)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -323,52 +381,58 @@ def run_ours(args, dist):
     dist.barrier()
 
     K = args.steps
-    inner = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in shapes] for _ in range(K)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(groups) + 1)]
+             for _ in range(K)]
     with ClockSampler(dev.index) as clocks:
         torch.cuda.synchronize()
         dist.barrier()
-        start.record(stream)
         for k in range(K):
-            one_step(inner[k])
-        end.record(stream)
+            one_step(marks[k])
         torch.cuda.synchronize()
     dist.barrier()
-    elapsed_ms = dist.max(start.elapsed_time(end), dev)
+    elapsed_ms = dist.max(marks[0][0].elapsed_time(marks[K - 1][len(groups)]), dev)
     ms_per_step = elapsed_ms / K
-    value = dist.world * step_bytes * K / (elapsed_ms / 1e3) / 1e9 if scaling == "weak" else \
-        sum(alg_bytes(r, h) for r, h in
-            (SHARD_SHAPES if args.workload == "shard" else shapes)) * K / (elapsed_ms / 1e3) / 1e9
+    total_bytes = dist.world * step_bytes if scaling == "weak" else \
+        sum(alg_bytes(r, h) for r, h in SHARD_SHAPES)
+    value = total_bytes * K / (elapsed_ms / 1e3) / 1e9
 
-    # ---- per-shape breakdown and roofline of the dominant kernel ----------
+    # ---- roofline of the dominant kernel (from the timed region) -----------
     peak, peak_src = measured_peak()
-    per_shape, by_plan = [], {}
-    for i, ((rows, h), plan) in enumerate(zip(shapes, plans)):
-        us = statistics.median(inner[k][i][0].elapsed_time(inner[k][i][1]) for k in range(K)) * 1e3
-        b = alg_bytes(rows, h)
-        entry = {"rows": rows, "hidden": h, "us": round(us, 2), "gbs": round(b / us / 1e3, 1),
-                 "frac": round(b / us / 1e3 / peak, 3), "plan": plan}
-        if args.workload == "sweep" and h in README_US:
-            entry["readme_us"] = README_US[h]
-        per_shape.append(entry)
-        kern = plan.split(":tpr")[0]
-        t, bb, n = by_plan.get(kern, (0.0, 0, 0))
-        by_plan[kern] = (t + us, bb + b, n + 1)
-    dom = max(by_plan, key=lambda k: by_plan[k][0])
-    t_us, b_dom, n_dom = by_plan[dom]
+    by_kern = {}
+    for g, (kern, idx) in enumerate(groups):
+        t = sum(marks[k][g].elapsed_time(marks[k][g + 1]) for k in range(K)) / K * 1e3
+        b = sum(alg_bytes(*shapes[i]) for i in idx)
+        t0, b0, n0 = by_kern.get(kern, (0.0, 0, 0))
+        by_kern[kern] = (t0 + t, b0 + b, n0 + len(idx))
+    dom = max(by_kern, key=lambda k: by_kern[k][0])
+    t_us, b_dom, n_dom = by_kern[dom]
     achieved = b_dom / t_us / 1e3
     traffic = None
     tr = committed_traffic()
     if tr:
-        vals = [tr.get(str(e["hidden"])) for e in per_shape if e["plan"].startswith(dom)]
+        vals = [tr.get(str(shapes[i][1])) for i, k in enumerate(kern_of) if k == dom]
         if vals and all(v is not None for v in vals):
             traffic = int(sum(vals) / len(vals))
     roofline = {"bound": "hbm", "kernel": dom, "launches_per_step": n_dom,
-                "time_share": round(t_us / sum(v[0] for v in by_plan.values()), 3),
+                "time_share": round(t_us / sum(v[0] for v in by_kern.values()), 3),
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 3), "peak_source": peak_src,
+                "avg_launch_us": round(t_us / n_dom, 2),
                 "algorithmic_bytes_per_launch": int(b_dom / n_dom), "traffic": traffic}
+
+    # ---- per-shape breakdown (after the timed region) ----------------------
+    # Each shape alone: a CUDA graph of back-to-back launches over enough
+    # rotating buffer sets (>= 600 MB) that every launch reads cold data.
+    per_shape = []
+    if not args.no_per_shape:
+        for i, (rows, h) in enumerate(shapes):
+            us = per_shape_us(torch, launch, i, rows, h, dev)
+            b = alg_bytes(rows, h)
+            entry = {"rows": rows, "hidden": h, "us": round(us, 2), "gbs": round(b / us / 1e3, 1),
+                     "frac": round(b / us / 1e3 / peak, 3), "plan": plans[i]}
+            if args.workload == "sweep" and h in README_US and rows == BATCH:
+                entry["readme_us"] = README_US[h]
+            per_shape.append(entry)
 
     line = {"metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": dist.world,
             "steps": K, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -382,9 +446,12 @@ def run_ours(args, dist):
                        "no collective"},
             "frac_of_peak": round(value / dist.world / peak, 3),
             "gpu_launches": K * len(shapes),
+            "gpu_launches_note": "one hprn_rms_norm kernel launch per shape per timed step",
             "roofline": roofline, "per_shape": per_shape,
+            "per_shape_method": ("CUDA-graph replay of back-to-back launches of one shape over "
+                                 "rotating buffer sets (>= 600 MB), cold L2"),
             "clocks": clocks.summary()}
-    if args.workload == "sweep":
+    if args.workload == "sweep" and shapes == [(BATCH, h) for h in SWEEP]:
         readme_gbs = sum(alg_bytes(BATCH, h) for h in SWEEP) / (sum(README_US.values()) * 1e3)
         line["vs_baseline"] = round(value / dist.world / readme_gbs, 3)
         line["baseline_note"] = ("vs_baseline = per-GPU value / the reference README's B200 "

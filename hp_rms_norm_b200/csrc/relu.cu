@@ -1,11 +1,11 @@
 // Elementwise ReLU for sm_100a and its C-ABI entry point.
 //
-// out = input < 0 ? +0 : input, on 16-bit floats, bit for bit like torch.relu
-// for every non-NaN value (-0.0 passes through, -inf becomes +0); NaNs pass
-// through with their input bits.  Two elements are handled per instruction
-// pair: `set.lt.u32.{bf16x2,f16x2}` produces an all-ones mask in each 16-bit
-// lane holding a value below zero (ordered compare, so NaN and -0.0 give 0),
-// and the lane is cleared with it.
+// out = input <= 0 ? +0 : input, on 16-bit floats: bit for bit what torch.relu
+// gives on CUDA for every non-NaN value (negatives, -inf and -0.0 all become
+// +0); NaNs pass through with their input bits.  Two elements are handled per
+// instruction pair: `set.le.u32.{bf16x2,f16x2}` produces an all-ones mask in
+// each 16-bit lane holding a value <= 0 (ordered compare, so NaN gives 0), and
+// the lane is cleared with it.
 //
 // Replaces the reference's activation kernel
 // (hp_rms_norm/csrc/cuda/activation_kernels.cuh:82-145), which moves 256 bytes
@@ -29,14 +29,14 @@ __device__ __forceinline__ uint32_t relu2(uint32_t w);
 template <>
 __device__ __forceinline__ uint32_t relu2<__nv_bfloat16>(uint32_t w) {
   uint32_t m;
-  asm("set.lt.u32.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(w), "r"(0u));
+  asm("set.le.u32.bf16x2 %0, %1, %2;" : "=r"(m) : "r"(w), "r"(0u));
   return w & ~m;
 }
 
 template <>
 __device__ __forceinline__ uint32_t relu2<__half>(uint32_t w) {
   uint32_t m;
-  asm("set.lt.u32.f16x2 %0, %1, %2;" : "=r"(m) : "r"(w), "r"(0u));
+  asm("set.le.u32.f16x2 %0, %1, %2;" : "=r"(m) : "r"(w), "r"(0u));
   return w & ~m;
 }
 

@@ -394,37 +394,57 @@ int choose_vec(int64_t hidden, int64_t rows, const void* x, const void* r, const
   return 2;
 }
 
+// Launch-plan heuristic, fitted to a cold-L2 sweep of every compiled plan on
+// B200 (batch 4096 bf16, hidden 1024..32768; the kernel timed as back-to-back
+// CUDA-graph launches over rotating buffers).  What won everywhere:
+//   * one CTA per row with as many threads as the row has 32-byte vectors
+//     (one vector per thread): the most warps per SM, so the most loads in
+//     flight, and the shortest serial chain per thread;
+//   * rows of at most 64 vectors: one warp per row, two rows per CTA;
+//   * rows of 1025..2048 vectors: two vectors per thread (four below ~1440
+//     vectors, where 1024-thread CTAs would leave SMs a CTA short);
+//   * thread-block clusters only once a row no longer fits one CTA: splitting
+//     rows that do fit cost 5-15% (cluster scheduling and the cluster barrier).
 Plan default_plan(int64_t rows, int nvec, int vec, const DeviceInfo& dev) {
+  (void)rows;
+  (void)dev;
   Plan p;
   p.vec = vec;
-  if (nvec <= 4 * 32) {
+  if (nvec <= 64) {
     p.kind = kWarpRows;
-    p.vpt = next_supported_vpt(kWarpRows, vec, (nvec + 31) / 32);
+    p.vpt = (nvec + 31) / 32;
     p.tpr = 32;
-    p.rows_per_cta = 4;
+    p.rows_per_cta = 2;
     return p;
   }
-  // One CTA (or cluster) per row: two vectors per thread, at most 256 threads
-  // per CTA, with the row split over a cluster once a CTA would exceed that.
-  int vpt = 2, cluster = 1;
-  auto per_cta_threads = [&](int c, int v) { return ((nvec + c - 1) / c + v - 1) / v; };
-  while (per_cta_threads(cluster, vpt) > 256 && cluster < 8) cluster *= 2;
-  // Short batches: spread rows over more SMs while each CTA keeps >= 2 warps of work.
-  while (rows * cluster < dev.sm_count && cluster < 8 && per_cta_threads(cluster * 2, vpt) >= 64)
-    cluster *= 2;
-  while (round_up(per_cta_threads(cluster, vpt), 32) > cta_max_threads(vpt) && vpt < 8)
-    vpt = next_supported_vpt(kCtaRows, vec, vpt + 1);
-  if (round_up(per_cta_threads(cluster, vpt), 32) > cta_max_threads(vpt)) {
-    p.kind = kTwoPass;
-    p.vpt = 4;
-    p.tpr = kTwoPassThreads;
-    p.cluster = 1;
+  if (nvec <= 1024) {
+    p.kind = kCtaRows;
+    p.vpt = 1;
+    p.tpr = round_up(nvec, 32);
     return p;
   }
-  p.kind = cluster > 1 ? kClusterRows : kCtaRows;
-  p.vpt = vpt;
-  p.cluster = cluster;
-  p.tpr = round_up(per_cta_threads(cluster, vpt), 32);
+  if (nvec <= 2048) {
+    p.kind = kCtaRows;
+    p.vpt = nvec <= 1440 ? 4 : 2;
+    p.tpr = round_up((nvec + p.vpt - 1) / p.vpt, 32);
+    return p;
+  }
+  // Longer rows: the smallest cluster (2, 4 or 8 CTAs) whose CTAs each hold at
+  // most 2048 vectors at two per thread; past 8 * 2048 vectors, two passes.
+  int cluster = 2;
+  while (cluster < 8 && (nvec + cluster - 1) / cluster > 2048) cluster *= 2;
+  const int slice = (nvec + cluster - 1) / cluster;
+  if (slice <= 2048) {
+    p.kind = kClusterRows;
+    p.cluster = cluster;
+    p.vpt = 2;
+    p.tpr = round_up((slice + 1) / 2, 32);
+    return p;
+  }
+  p.kind = kTwoPass;
+  p.vpt = 4;
+  p.tpr = kTwoPassThreads;
+  p.cluster = 1;
   return p;
 }
 
@@ -593,6 +613,10 @@ int validate(const Problem& q) {
     }
     if (!disjoint_rows) return fail(HPRN_ERR_INVALID_ARGUMENT, "input and residual must not overlap");
   }
+  // The weight is read through the non-coherent cache: it must not be written by this call.
+  const char* wb = static_cast<const char*>(q.w);
+  if ((wb < xb + 2 * xspan && xb < wb + 2 * q.hidden) || (wb < rb + 2 * rspan && rb < wb + 2 * q.hidden))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "weight must not overlap input or residual");
   return HPRN_OK;
 }
 

@@ -72,8 +72,9 @@ HPRN_API int hprn_rms_norm(void* input, const void* weight, void* residual, int6
                            double eps, int dtype, void* stream);
 
 /*
- * Elementwise ReLU, out-of-place: out[i, :] = input[i, :] < 0 ? +0 : input[i, :]
- * (torch.relu: -0.0 and NaN pass through with their bits unchanged, -inf -> +0).
+ * Elementwise ReLU, out-of-place: out[i, :] = input[i, :] <= 0 ? +0 : input[i, :]
+ * (torch.relu as computed on CUDA, bit for bit: negatives, -inf and -0.0 give
+ * +0; NaNs pass through with their input bits).
  * out and input may be the same pointer (in place) but must not otherwise overlap.
  *
  * Replaces the reference's

@@ -25,8 +25,10 @@
  * as any fp32-accumulating kernel.  The output product is then formed in float,
  * left to right, exactly as hp_rms_norm.cuh:108-109 writes it.
  *
- * ReLU follows torch.relu bit for bit: x < 0 ? +0 : x, so -0.0 and NaN pass
- * through unchanged and -inf becomes +0.  (The reference's "relu" kernel,
+ * ReLU follows torch.relu as computed on CUDA, bit for bit: x <= 0 ? +0 : x,
+ * so negatives, -inf and -0.0 become +0 and NaNs pass through with their bits
+ * (torch's CPU kernel differs in keeping -0.0 and rewriting NaN payloads).
+ * (The reference's "relu" kernel,
  * hp_rms_norm/csrc/cuda/activation_kernels.cuh:99-119, is a plain copy; the
  * product follows torch.relu instead.)
  *
@@ -54,11 +56,12 @@ static inline float bf16_to_f32(uint16_t b) {
   return f;
 }
 
-/* Round to nearest, ties to even.  NaN maps to the canonical quiet NaN. */
+/* Round to nearest, ties to even.  NaN maps to 0x7fff, the canonical NaN the
+ * GPU's cvt.rn.bf16.f32 produces. */
 static inline uint16_t f32_to_bf16_rn(float f) {
   uint32_t u;
   memcpy(&u, &f, 4);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)(((u >> 16) & 0x8000u) | 0x7fc0u);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)0x7fffu;
   u += 0x7fffu + ((u >> 16) & 1u);
   return (uint16_t)(u >> 16);
 }
@@ -72,6 +75,7 @@ static inline float f16_to_f32(uint16_t b) {
 }
 
 static inline uint16_t f32_to_f16_rn(float f) {
+  if (f != f) return (uint16_t)0x7fffu; /* the GPU's canonical NaN (cvt.rn.f16.f32) */
   _Float16 h = (_Float16)f;
   uint16_t b;
   memcpy(&b, &h, 2);
@@ -131,15 +135,16 @@ void oracle_fused_add_rms_norm(int dtype, uint16_t* input, const uint16_t* weigh
   }
 }
 
-/* torch.relu on raw 16-bit patterns: negative finite values and -inf become +0. */
+/* torch.relu (CUDA) on raw 16-bit patterns: every value <= 0 (negatives, -inf,
+ * -0.0) becomes +0; NaNs and positives pass through unchanged. */
 void oracle_relu(int dtype, uint16_t* out, const uint16_t* in, int64_t n) {
   const uint16_t inf_bits = dtype == ORACLE_BF16 ? 0x7f80u : 0x7c00u;
 #pragma omp parallel for schedule(static)
   for (int64_t i = 0; i < n; ++i) {
     uint16_t b = in[i];
     uint16_t mag = (uint16_t)(b & 0x7fffu);
-    int negative = (b & 0x8000u) && mag != 0 && mag <= inf_bits; /* not -0, not NaN */
-    out[i] = negative ? (uint16_t)0 : b;
+    int non_positive = (b & 0x8000u) && mag <= inf_bits; /* sign set, not NaN */
+    out[i] = non_positive ? (uint16_t)0 : b;
   }
 }
 

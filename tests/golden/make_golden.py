@@ -14,7 +14,9 @@ PyTorch formula is executed.
 ReLU fixtures (``relu_golden.npz``) come from ``torch.relu`` on CPU, the oracle
 for that op (the reference's own ``relu`` kernel is a copy: its test,
 test/test_relu.py:24, asserts ``out == input``).  Special values (signed zeros,
-infinities, NaNs with payloads, subnormals) are included.
+infinities, NaNs with payloads, subnormals) are included.  torch.relu on CPU
+keeps -0.0 and rewrites NaN payloads, where torch.relu on CUDA (which the
+product follows) gives +0 for -0.0; the tests compare around those two.
 
 The fixtures are small (about 2 MB) and are committed; tests read only
 them, never the reference tree.

@@ -40,9 +40,9 @@ def test_version_and_status_strings():
 
 
 @pytest.mark.parametrize("rows,hidden,kind", [
-    (4096, 1024, "warp"), (4096, 2048, "warp"), (4096, 4096, "cta"), (4096, 8192, "cta"),
-    (4096, 16384, "cluster"), (4096, 32768, "cluster"), (1, 8192, "cluster"),
-    (3, 1 << 22, "twopass"),
+    (4096, 1024, "warp"), (4096, 2048, "cta"), (4096, 4096, "cta"), (4096, 8192, "cta"),
+    (4096, 16384, "cta"), (4096, 32768, "cta"), (1, 8192, "cta"), (4, 65536, "cluster"),
+    (4, 1 << 18, "cluster"), (3, 1 << 22, "twopass"),
 ])
 def test_plan_kinds(rows, hidden, kind):
     p = capi.plan(rows, hidden)
@@ -100,6 +100,8 @@ def test_rms_norm_argument_errors_before_any_launch():
                  capi.ERR_INVALID_ARGUMENT, "overlap")
     expect_error(lambda: capi.rms_norm(F, F, F, 4, 8, 8, 8, 1e-6, bf),
                  capi.ERR_INVALID_ARGUMENT, "overlap")
+    expect_error(lambda: capi.rms_norm(F, F + 16, 2 * F, 4, 8, 8, 8, 1e-6, bf),
+                 capi.ERR_INVALID_ARGUMENT, "weight must not overlap")
 
 
 def test_rms_norm_zero_rows_is_a_no_op():

@@ -35,13 +35,19 @@ def test_every_bit_pattern(cuda, dtype):
 
 
 def test_golden_fixture(cuda, relu_golden):
+    """CPU torch.relu fixtures: bit-exact except -0.0 (CUDA's torch.relu, which the
+    kernel follows, gives +0) and NaN payloads (kept by the kernel)."""
     for name in ("bf16", "fp16"):
         tdtype, code = DTYPES[name]
         xb, want = relu_golden[name]
         x = from_bits(xb, tdtype, cuda)
         out = torch.zeros_like(x)
         run(out, x)
-        assert_bits_equal(bits(out), want, code, label=name, nan_payload=False)
+        got = bits(out).reshape(-1)
+        xb, want = xb.reshape(-1), want.reshape(-1)
+        keep = ~is_nan(xb, code) & (xb != 0x8000)
+        assert_bits_equal(got[keep], want[keep], code, label=name)
+        assert_bits_equal(got, O.relu(code, xb), code, label=name + " vs oracle")
 
 
 @pytest.mark.parametrize("shape,dtype", [((4096, 14336), "bf16"), ((8192, 28672), "fp16")])
