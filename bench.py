@@ -324,10 +324,12 @@ def run_ours(args, dist):
         workload = f"config0: fused add+RMSNorm {args.rows} x 4096 bf16"
     elif args.workload == "shard":
         scaling = "strong"
+        from hp_rms_norm_b200.shard import row_range
+
         shapes = []
         for rows, h in SHARD_SHAPES:
-            per = rows // dist.world
-            shapes.append((per + (1 if dist.rank < rows % dist.world else 0), h))
+            start, stop = row_range(rows, dist.world, dist.rank)
+            shapes.append((stop - start, h))
         workload = ("config4: global 65536 x 8192 and 32768 x 32768 bf16, rows split evenly "
                     "across ranks, no collective")
     elif args.workload == "decode":
