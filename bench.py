@@ -264,6 +264,16 @@ def per_shape_us(torch, launch, i, rows, h, dev, min_bytes=600e6, reps=3):
     return e0.elapsed_time(e1) * 1e3 / (reps * L)
 
 
+def host_threads() -> int:
+    """All host threads this process may use (torchrun sets OMP_NUM_THREADS=1
+    per rank; the CPU legs run on one rank only, so they take the lot)."""
+    import torch
+
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    torch.set_num_threads(n)
+    return n
+
+
 def cpu_eager_sample(shapes, seconds: float):
     """Times the reference formula on the host cores over a bounded sample.
 
@@ -272,7 +282,7 @@ def cpu_eager_sample(shapes, seconds: float):
 
     from oracle import oracle as O
 
-    threads = torch.get_num_threads()
+    threads = host_threads()
     g = torch.Generator().manual_seed(0)
     data = []
     for rows, hidden in shapes:
@@ -607,6 +617,7 @@ def run_reference(args, dist):
         for x, w, r in data:
             O.eager_formula(x, r, w, 1e-6)
 
+    threads = host_threads()
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
@@ -614,7 +625,6 @@ def run_reference(args, dist):
         step()
     el = time.perf_counter() - t0
     value = step_bytes * args.steps / el / 1e9
-    threads = torch.get_num_threads()
     desc = (f"reference eager formula (test/test_hp_rms_norm.py:6-19, restated in oracle/oracle.py) "
             f"on {threads} host threads; each step = {sample_rows} rows at each of the "
             f"{len(shapes)} shapes of the workload")

@@ -22,10 +22,15 @@ ERR_UNSUPPORTED_DTYPE = -2
 ERR_UNSUPPORTED_DEVICE = -3
 ERR_CUDA = -4
 
+LAUNCH_PDL = 1
+LAUNCH_DEFAULT = LAUNCH_PDL
+
 # Every symbol include/hp_rms_norm_b200.h declares.
 EXPORTED = (
     "hprn_rms_norm",
     "hprn_relu",
+    "hprn_rms_norm_ex",
+    "hprn_relu_ex",
     "hprn_last_error",
     "hprn_status_string",
     "hprn_version",
@@ -50,7 +55,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         return _lib
     if not os.path.exists(path):
         raise ImportError(
-            f"{path} is missing: build it with `python -m hp_rms_norm_b200.build` "
+            f"{path} is missing: build it with `python hp_rms_norm_b200/build.py` "
             "(the CUDA library is required; there is no CPU fallback)")
     lib = ctypes.CDLL(path)
     vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
@@ -58,6 +63,11 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_rms_norm.restype = c_int
     lib.hprn_relu.argtypes = [vp, vp, i64, i64, i64, i64, c_int, vp]
     lib.hprn_relu.restype = c_int
+    u32 = ctypes.c_uint
+    lib.hprn_rms_norm_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, ctypes.c_double, c_int, vp, u32]
+    lib.hprn_rms_norm_ex.restype = c_int
+    lib.hprn_relu_ex.argtypes = [vp, vp, i64, i64, i64, i64, c_int, vp, u32]
+    lib.hprn_relu_ex.restype = c_int
     lib.hprn_last_error.argtypes = []
     lib.hprn_last_error.restype = ctypes.c_char_p
     lib.hprn_status_string.argtypes = [c_int]
@@ -80,15 +90,29 @@ def _check(status: int) -> None:
 
 def rms_norm(input_ptr: int, weight_ptr: int, residual_ptr: int, rows: int, hidden: int,
              input_row_stride: int, residual_row_stride: int, eps: float, dtype: int,
-             stream: int = 0) -> None:
-    _check(load().hprn_rms_norm(input_ptr, weight_ptr, residual_ptr, rows, hidden,
-                                input_row_stride, residual_row_stride, eps, dtype, stream))
+             stream: int = 0, flags: int | None = None) -> None:
+    """hprn_rms_norm, or hprn_rms_norm_ex when launch `flags` are given."""
+    lib = load()
+    if flags is None:
+        st = lib.hprn_rms_norm(input_ptr, weight_ptr, residual_ptr, rows, hidden,
+                               input_row_stride, residual_row_stride, eps, dtype, stream)
+    else:
+        st = lib.hprn_rms_norm_ex(input_ptr, weight_ptr, residual_ptr, rows, hidden,
+                                  input_row_stride, residual_row_stride, eps, dtype, stream, flags)
+    _check(st)
 
 
 def relu(out_ptr: int, input_ptr: int, rows: int, hidden: int, out_row_stride: int,
-         input_row_stride: int, dtype: int, stream: int = 0) -> None:
-    _check(load().hprn_relu(out_ptr, input_ptr, rows, hidden, out_row_stride, input_row_stride,
-                            dtype, stream))
+         input_row_stride: int, dtype: int, stream: int = 0, flags: int | None = None) -> None:
+    """hprn_relu, or hprn_relu_ex when launch `flags` are given."""
+    lib = load()
+    if flags is None:
+        st = lib.hprn_relu(out_ptr, input_ptr, rows, hidden, out_row_stride, input_row_stride,
+                           dtype, stream)
+    else:
+        st = lib.hprn_relu_ex(out_ptr, input_ptr, rows, hidden, out_row_stride,
+                              input_row_stride, dtype, stream, flags)
+    _check(st)
 
 
 def plan(rows: int, hidden: int, dtype: int = DTYPE_BF16, input_ptr: int = 0,
@@ -121,7 +145,8 @@ def dtype_code(t) -> int:
     raise HprnError(ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16")
 
 
-def rms_norm_tensors(inp, weight, res, eps: float, stream: int | None = None) -> None:
+def rms_norm_tensors(inp, weight, res, eps: float, stream: int | None = None,
+                     flags: int | None = None) -> None:
     """C-ABI call on 2-D CUDA tensors (row stride from the tensors)."""
     import torch
 
@@ -129,14 +154,14 @@ def rms_norm_tensors(inp, weight, res, eps: float, stream: int | None = None) ->
         stream = torch.cuda.current_stream(inp.device).cuda_stream
     rows, hidden = inp.shape
     rms_norm(inp.data_ptr(), weight.data_ptr(), res.data_ptr(), rows, hidden, inp.stride(0),
-             res.stride(0), eps, dtype_code(inp), stream)
+             res.stride(0), eps, dtype_code(inp), stream, flags)
 
 
-def relu_tensors(out, inp, stream: int | None = None) -> None:
+def relu_tensors(out, inp, stream: int | None = None, flags: int | None = None) -> None:
     import torch
 
     if stream is None:
         stream = torch.cuda.current_stream(inp.device).cuda_stream
     rows, hidden = inp.shape
     relu(out.data_ptr(), inp.data_ptr(), rows, hidden, out.stride(0), inp.stride(0),
-         dtype_code(inp), stream)
+         dtype_code(inp), stream, flags)

@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(256) relu_rows(ReluArgs a) {
   uint16_t* dst = a.out + row * a.out_stride;
   const uint64_t pol = policy_evict_first();
   const int64_t base = chunk * (static_cast<int64_t>(blockDim.x) * U) + threadIdx.x;
+  pdl_entry();
 
   Vec<VEC> v[U];
 #pragma unroll
@@ -117,7 +118,16 @@ extern "C" {
 
 int hprn_relu(void* out, const void* input, int64_t rows, int64_t hidden, int64_t out_row_stride,
               int64_t input_row_stride, int dtype, void* stream) {
+  return hprn_relu_ex(out, input, rows, hidden, out_row_stride, input_row_stride, dtype, stream,
+                      HPRN_LAUNCH_DEFAULT);
+}
+
+int hprn_relu_ex(void* out, const void* input, int64_t rows, int64_t hidden,
+                 int64_t out_row_stride, int64_t input_row_stride, int dtype, void* stream,
+                 unsigned flags) {
   using namespace hprn;
+  if (flags & ~static_cast<unsigned>(HPRN_LAUNCH_PDL))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown launch flags");
   if (dtype != HPRN_DTYPE_BF16 && dtype != HPRN_DTYPE_FP16)
     return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
   if (rows < 0 || hidden < 0) return fail(HPRN_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
@@ -173,8 +183,22 @@ int hprn_relu(void* out, const void* input, int64_t rows, int64_t hidden, int64_
   const int64_t grid = a.rows * a.chunks_per_row;
   if (grid > 2147483647LL) return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor too large for one launch");
   ReluFn fn = dtype == HPRN_DTYPE_BF16 ? pick_relu<__nv_bfloat16>(vec) : pick_relu<__half>(vec);
-  fn<<<static_cast<unsigned>(grid), kReluThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  return check_launch("relu");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kReluThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 0;
+  if (flags & HPRN_LAUNCH_PDL) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+  if (e != cudaSuccess)
+    return fail(HPRN_ERR_CUDA, std::string("relu launch failed: ") + cudaGetErrorString(e));
+  return ok();
 }
 
 }  // extern "C"

@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + (threadIdx.x >> 5);
+  pdl_entry();
   if (row >= a.rows) return;
   uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = a.r + row * a.r_stride;
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   int64_t row;
   int v_begin = 0, v_end = a.nvec;
   uint32_t crank = 0, csize = 1;
+  pdl_entry();
   if constexpr (CLUSTER) {
     // Phase 1 of the cluster barrier: completes once every CTA of the cluster
     // is running, which makes their shared memory safe to write.
@@ -284,6 +286,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   uint16_t* rr = a.r + row * a.r_stride;
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
+  pdl_entry();
 
   float a0 = 0.f, a1 = 0.f;
   for (int base = 0; base < a.nvec; base += U * nthreads) {
@@ -655,7 +658,7 @@ int make_plan(const Problem& q, const DeviceInfo& dev, Plan* plan, RmsArgs* args
   return HPRN_OK;
 }
 
-int launch(const Plan& p, RmsArgs a, int dtype, cudaStream_t stream) {
+int launch(const Plan& p, RmsArgs a, int dtype, cudaStream_t stream, unsigned flags) {
   KernelFn fn = pick_kernel(dtype, p);
   if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
   // Rows handled per CTA-group in grid.x; split very tall problems into launches.
@@ -671,19 +674,24 @@ int launch(const Plan& p, RmsArgs a, int dtype, cudaStream_t stream) {
     c.rows = n;
     const int64_t units = (n + rows_per_unit - 1) / rows_per_unit;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(static_cast<unsigned>(units * ctas_per_unit), 1, 1);
     cfg.blockDim = dim3(p.kind == kWarpRows ? 32 * p.rows_per_cta : p.tpr, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
+    cfg.attrs = attr;
     cfg.numAttrs = 0;
     if (p.kind == kClusterRows) {
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = p.cluster;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
+      attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+      attr[cfg.numAttrs].val.clusterDim.x = p.cluster;
+      attr[cfg.numAttrs].val.clusterDim.y = 1;
+      attr[cfg.numAttrs].val.clusterDim.z = 1;
+      ++cfg.numAttrs;
+    }
+    if (flags & HPRN_LAUNCH_PDL) {
+      attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+      ++cfg.numAttrs;
     }
     cudaError_t e = cudaLaunchKernelEx(&cfg, fn, c);
     if (e != cudaSuccess)
@@ -701,7 +709,16 @@ extern "C" {
 int hprn_rms_norm(void* input, const void* weight, void* residual, int64_t rows, int64_t hidden,
                   int64_t input_row_stride, int64_t residual_row_stride, double eps, int dtype,
                   void* stream) {
+  return hprn_rms_norm_ex(input, weight, residual, rows, hidden, input_row_stride,
+                          residual_row_stride, eps, dtype, stream, HPRN_LAUNCH_DEFAULT);
+}
+
+int hprn_rms_norm_ex(void* input, const void* weight, void* residual, int64_t rows,
+                     int64_t hidden, int64_t input_row_stride, int64_t residual_row_stride,
+                     double eps, int dtype, void* stream, unsigned flags) {
   using namespace hprn;
+  if (flags & ~static_cast<unsigned>(HPRN_LAUNCH_PDL))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown launch flags");
   Problem q{input, weight, residual, rows, hidden, input_row_stride, residual_row_stride, eps, dtype};
   int st = validate(q);
   if (st != HPRN_OK) return st;
@@ -711,7 +728,7 @@ int hprn_rms_norm(void* input, const void* weight, void* residual, int64_t rows,
   Plan p;
   RmsArgs a;
   if ((st = make_plan(q, *dev, &p, &a)) != HPRN_OK) return st;
-  if ((st = launch(p, a, dtype, static_cast<cudaStream_t>(stream))) != HPRN_OK) return st;
+  if ((st = launch(p, a, dtype, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK) return st;
   return ok();
 }
 

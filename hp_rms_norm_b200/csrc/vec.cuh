@@ -287,4 +287,16 @@ __device__ __forceinline__ uint16_t pack1<__half>(float f) {
   return __half_as_ushort(__float2half_rn(f));
 }
 
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel calls both at entry, before its
+// first global-memory access: launch_dependents lets a following kernel that
+// was launched with programmatic stream serialization start being scheduled
+// once all of this grid's CTAs are running, and wait blocks until the grid
+// this one depends on (if it was launched that way) has completed and its
+// memory is visible.  With no programmatic dependency both are no-ops.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 }  // namespace hprn

@@ -40,6 +40,18 @@ typedef enum hprn_dtype {
   HPRN_DTYPE_FP16 = 1  /* torch.float16  / __half        */
 } hprn_dtype;
 
+/*
+ * Launch flags for the *_ex entry points.
+ *   HPRN_LAUNCH_PDL: launch with programmatic stream serialization (programmatic
+ *   dependent launch).  The kernel may then be scheduled while the previous
+ *   kernel on the stream is still finishing; it waits (griddepcontrol.wait)
+ *   for that kernel to complete before its first memory access, so results
+ *   are the same as a plain launch.  Every kernel of this library also allows
+ *   its own successor to start early in the same way.
+ */
+#define HPRN_LAUNCH_PDL 1u
+#define HPRN_LAUNCH_DEFAULT HPRN_LAUNCH_PDL
+
 typedef enum hprn_status {
   HPRN_OK = 0,
   HPRN_ERR_INVALID_ARGUMENT = -1, /* bad size, stride, null pointer, overlap */
@@ -87,6 +99,19 @@ HPRN_API int hprn_rms_norm(void* input, const void* weight, void* residual, int6
  */
 HPRN_API int hprn_relu(void* out, const void* input, int64_t rows, int64_t hidden,
                        int64_t out_row_stride, int64_t input_row_stride, int dtype, void* stream);
+
+/*
+ * hprn_rms_norm and hprn_relu with explicit launch flags (HPRN_LAUNCH_*; 0 for
+ * a plain launch).  The plain entry points use HPRN_LAUNCH_DEFAULT.
+ * (Extensions of the reference's fixed launch: FlashInfer-style enable_pdl.)
+ */
+HPRN_API int hprn_rms_norm_ex(void* input, const void* weight, void* residual, int64_t rows,
+                              int64_t hidden, int64_t input_row_stride,
+                              int64_t residual_row_stride, double eps, int dtype, void* stream,
+                              unsigned flags);
+HPRN_API int hprn_relu_ex(void* out, const void* input, int64_t rows, int64_t hidden,
+                          int64_t out_row_stride, int64_t input_row_stride, int dtype,
+                          void* stream, unsigned flags);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 HPRN_API const char* hprn_last_error(void);

@@ -263,3 +263,45 @@ def test_matches_reference_cuda_kernel(cuda, hidden):
     run_capi(x, w, r, eps)
     assert torch.equal(r.view(torch.int16), rr.view(torch.int16))
     assert int(ulp_distance(x, xr).max()) <= 1
+
+
+@pytest.mark.parametrize("hidden", [1024, 4096, 20480, 65536])
+def test_pdl_chains_match_plain_launches(cuda, hidden):
+    """Back-to-back dependent launches (each call reads the previous call's
+    output, then ReLU reads the last output) give the same bits with
+    programmatic dependent launch as with plain launches, eagerly and inside a
+    CUDA graph."""
+    rows = 64 if hidden > 32768 else 512
+    x0, w, r0, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=hidden + 7, device=cuda)
+
+    def chain(x, r, out, flags, stream):
+        for _ in range(3):
+            capi.rms_norm_tensors(x, w, r, eps, stream=stream, flags=flags)
+        capi.relu_tensors(out, x, stream=stream, flags=flags)
+
+    results = []
+    for flags in (0, capi.LAUNCH_PDL):
+        x, r, out = x0.clone(), r0.clone(), torch.empty_like(x0)
+        chain(x, r, out, flags, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        results.append((x, r, out))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    xg, rg, og = x0.clone(), r0.clone(), torch.empty_like(x0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        chain(xg, rg, og, capi.LAUNCH_PDL, s.cuda_stream)
+    xg.copy_(x0)
+    rg.copy_(r0)
+    g.replay()
+    torch.cuda.synchronize()
+    results.append((xg, rg, og))
+    for got in results[1:]:
+        for a, b in zip(results[0], got):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_launch_flags_validated(cuda):
+    x, w, r, eps = make_inputs(4, 256, torch.bfloat16, "c0", seed=1, device=cuda)
+    with pytest.raises(capi.HprnError, match="unknown launch flags"):
+        capi.rms_norm_tensors(x, w, r, eps, flags=0x80)
