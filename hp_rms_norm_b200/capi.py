@@ -25,12 +25,17 @@ ERR_CUDA = -4
 LAUNCH_PDL = 1
 LAUNCH_DEFAULT = LAUNCH_PDL
 
+OUT_SAME = 0
+OUT_FP8_E4M3_STATIC = 1
+OUT_FP8_E4M3_DYNAMIC = 2
+
 # Every symbol include/hp_rms_norm_b200.h declares.
 EXPORTED = (
     "hprn_rms_norm",
     "hprn_relu",
     "hprn_rms_norm_ex",
     "hprn_relu_ex",
+    "hprn_rms_norm_out",
     "hprn_last_error",
     "hprn_status_string",
     "hprn_version",
@@ -68,6 +73,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_rms_norm_ex.restype = c_int
     lib.hprn_relu_ex.argtypes = [vp, vp, i64, i64, i64, i64, c_int, vp, u32]
     lib.hprn_relu_ex.restype = c_int
+    lib.hprn_rms_norm_out.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, ctypes.c_double,
+                                      c_int, c_int, vp, vp, vp, u32]
+    lib.hprn_rms_norm_out.restype = c_int
     lib.hprn_last_error.argtypes = []
     lib.hprn_last_error.restype = ctypes.c_char_p
     lib.hprn_status_string.argtypes = [c_int]
@@ -113,6 +121,16 @@ def relu(out_ptr: int, input_ptr: int, rows: int, hidden: int, out_row_stride: i
         st = lib.hprn_relu_ex(out_ptr, input_ptr, rows, hidden, out_row_stride,
                               input_row_stride, dtype, stream, flags)
     _check(st)
+
+
+def rms_norm_out(out_ptr: int, input_ptr: int, weight_ptr: int, residual_ptr: int | None,
+                 rows: int, hidden: int, out_row_stride: int, input_row_stride: int,
+                 residual_row_stride: int, eps: float, dtype: int, out_form: int = OUT_SAME,
+                 scale_ptr: int | None = None, row_scales_ptr: int | None = None,
+                 stream: int = 0, flags: int = LAUNCH_DEFAULT) -> None:
+    _check(load().hprn_rms_norm_out(out_ptr, input_ptr, weight_ptr, residual_ptr, rows, hidden,
+                                    out_row_stride, input_row_stride, residual_row_stride, eps,
+                                    dtype, out_form, scale_ptr, row_scales_ptr, stream, flags))
 
 
 def plan(rows: int, hidden: int, dtype: int = DTYPE_BF16, input_ptr: int = 0,
@@ -165,3 +183,24 @@ def relu_tensors(out, inp, stream: int | None = None, flags: int | None = None) 
     rows, hidden = inp.shape
     relu(out.data_ptr(), inp.data_ptr(), rows, hidden, out.stride(0), inp.stride(0),
          dtype_code(inp), stream, flags)
+
+
+def rms_norm_out_tensors(out, inp, weight, res, eps: float, scale=None, row_scales=None,
+                         stream: int | None = None, flags: int = LAUNCH_DEFAULT) -> None:
+    """hprn_rms_norm_out on 2-D CUDA tensors; `res` may be None (plain RMSNorm).
+    The output form follows out's dtype (16-bit: same; float8_e4m3fn: static
+    with `scale`, dynamic with `row_scales`)."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(inp.device).cuda_stream
+    rows, hidden = inp.shape
+    if out.dtype == torch.float8_e4m3fn:
+        form = OUT_FP8_E4M3_STATIC if scale is not None else OUT_FP8_E4M3_DYNAMIC
+    else:
+        form = OUT_SAME
+    rms_norm_out(out.data_ptr(), inp.data_ptr(), weight.data_ptr(),
+                 res.data_ptr() if res is not None else None, rows, hidden, out.stride(0),
+                 inp.stride(0), res.stride(0) if res is not None else hidden, eps, dtype_code(inp),
+                 form, scale.data_ptr() if scale is not None else None,
+                 row_scales.data_ptr() if row_scales is not None else None, stream, flags)

@@ -1,13 +1,22 @@
-// Fused residual-add + RMSNorm for sm_100a, and its C-ABI entry point.
+// Fused residual-add + RMSNorm (and its plain / fp8-output forms) for sm_100a,
+// and the C-ABI entry points.
 //
 // Per row i (hidden elements, 16-bit storage T, fp32 arithmetic):
 //   s_j   = f32(x_ij) + f32(r_ij)
 //   r_ij <- round_T(s_j)
 //   inv   = rsqrt(eps + sum_j s_j^2 / hidden)          (s_j before rounding)
-//   x_ij <- round_T(f32(r_ij) * f32(w_j) * inv)
+//   y_ij  = f32(r_ij) * f32(w_j) * inv
+//   x_ij <- round_T(y_ij)
 // which is the arithmetic of the reference kernel
 // (hp_rms_norm/csrc/cuda/hp_rms_norm.cuh:186-207 for the add and the sum of
 // squares, :231 for the inverse RMS, :104-110 for the output product).
+//
+// Beyond the reference's one in-place form, the same kernels compute
+//   * plain RMSNorm (no residual: s_j = f32(x_ij), y uses f32(x_ij)),
+//   * the result into a separate output tensor (input left unchanged),
+//   * an fp8 e4m3 output: e4m3_satfinite(y * (1 / scale)) with a static
+//     per-tensor scale, or with a per-row scale max_j |y_ij| / 448 that is
+//     also written out (dynamic per-token quantisation).
 //
 // The work is purely HBM-bound (8 bytes moved per element, ~6 flops), so the
 // kernels are built to keep HBM busy:
@@ -22,10 +31,10 @@
 //     barrier at all), one CTA, or a thread-block cluster of up to 8 CTAs
 //     whose partial sums meet in distributed shared memory, so that CTAs stay
 //     small enough for many to be resident per SM at every hidden size (no
-//     occupancy cliff at large hidden, and short batches still spread over
-//     many SMs);
+//     occupancy cliff at large hidden);
 //   * rows too long for the register-resident kernels use a two-pass kernel
 //     that re-reads its own just-written residual from L2, not HBM.
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -39,13 +48,27 @@
 
 namespace hprn {
 
+// What a launch writes.
+enum OutForm : int {
+  kOutSame = HPRN_OUT_SAME,                   // 16-bit T into `out` (may be the input)
+  kOutFp8Static = HPRN_OUT_FP8_E4M3_STATIC,   // e4m3 with one scale for the tensor
+  kOutFp8Dynamic = HPRN_OUT_FP8_E4M3_DYNAMIC  // e4m3 with one scale per row, written out
+};
+
+constexpr float kE4m3Max = 448.0f;
+constexpr float kMinAmax = 1e-12f;
+
 struct RmsArgs {
-  uint16_t* x;         // input, overwritten with the output
+  const uint16_t* x;   // input rows
   const uint16_t* w;   // weight [hidden]
-  uint16_t* r;         // residual, overwritten with input + residual
+  uint16_t* r;         // residual rows, updated in place (null: plain RMSNorm)
+  void* out;           // output rows (T or e4m3 bytes)
+  const float* scale;  // static fp8 scale (one float)
+  float* row_scales;   // dynamic fp8 scales, one per row
   int64_t rows;
   int64_t x_stride;    // elements between rows
   int64_t r_stride;
+  int64_t out_stride;
   int32_t nvec;        // vectors per row (hidden / elements-per-vector)
   int32_t slice_vecs;  // vectors per CTA when a cluster splits the row
   int32_t rows_per_cta;
@@ -75,6 +98,22 @@ __device__ __forceinline__ void add_round(Vec<VEC>& xv, const Vec<VEC>& rv, floa
   }
 }
 
+// Sum of squares of the input alone (plain RMSNorm).
+template <typename T, int VEC>
+__device__ __forceinline__ void square_sum(const Vec<VEC>& xv, float& a0, float& a1) {
+  if constexpr (VEC == 2) {
+    const float s = unpack1<T>(xv.h);
+    a0 = fmaf(s, s, a0);
+  } else {
+#pragma unroll
+    for (int k = 0; k < Vec<VEC>::kWords; ++k) {
+      const float2 a = unpack2<T>(xv.w[k]);
+      a0 = fmaf(a.x, a.x, a0);
+      a1 = fmaf(a.y, a.y, a1);
+    }
+  }
+}
+
 // round_T((f32(r) * f32(w)) * inv), multiplied in the reference's order.
 template <typename T, int VEC>
 __device__ __forceinline__ Vec<VEC> normalize(const Vec<VEC>& rv, const Vec<VEC>& wv, float inv) {
@@ -92,10 +131,53 @@ __device__ __forceinline__ Vec<VEC> normalize(const Vec<VEC>& rv, const Vec<VEC>
   return o;
 }
 
-// Butterfly sum: every lane ends with the same bits.
+// max_j |y_j| over one vector, folded into m (NaNs are ignored, as by fmaxf).
+template <typename T, int VEC>
+__device__ __forceinline__ float vec_amax(const Vec<VEC>& rv, const Vec<VEC>& wv, float inv,
+                                          float m) {
+#pragma unroll
+  for (int k = 0; k < Vec<VEC>::kWords; ++k) {
+    const float2 a = unpack2<T>(rv.w[k]);
+    const float2 b = unpack2<T>(wv.w[k]);
+    m = fmaxf(m, fabsf(a.x * b.x * inv));
+    m = fmaxf(m, fabsf(a.y * b.y * inv));
+  }
+  return m;
+}
+
+// e4m3_satfinite((f32(r) * f32(w) * inv) * inv_scale) for one vector: VEC/2
+// output bytes, element order preserved.
+template <typename T, int VEC>
+__device__ __forceinline__ Vec<VEC / 2> quantize_e4m3(const Vec<VEC>& rv, const Vec<VEC>& wv,
+                                                      float inv, float inv_scale) {
+  static_assert(VEC >= 8, "fp8 output needs at least 4 elements per vector");
+  Vec<VEC / 2> o;
+#pragma unroll
+  for (int k = 0; k < Vec<VEC>::kWords; k += 2) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float2 a = unpack2<T>(rv.w[k + h]);
+      const float2 b = unpack2<T>(wv.w[k + h]);
+      const float2 q = make_float2(a.x * b.x * inv * inv_scale, a.y * b.y * inv * inv_scale);
+      const __nv_fp8x2_storage_t p = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
+      word |= static_cast<uint32_t>(p) << (16 * h);
+    }
+    o.w[k / 2] = word;
+  }
+  return o;
+}
+
+// Butterfly reductions: every lane ends with the same bits.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
 
@@ -137,19 +219,41 @@ __device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, floa
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
+// Inverse of the static fp8 scale, read after the programmatic-launch wait.
+template <int OUT>
+__device__ __forceinline__ float static_inv_scale(const RmsArgs& a) {
+  if constexpr (OUT == kOutFp8Static) return 1.0f / __ldg(a.scale);
+  return 1.0f;
+}
+
+// Writes one output vector of row `row` at vector index v.
+template <typename T, int VEC, int OUT>
+__device__ __forceinline__ void store_out(const RmsArgs& a, int64_t row, int64_t v,
+                                          const Vec<VEC>& rv, const Vec<VEC>& wv, float inv,
+                                          float inv_scale) {
+  constexpr int EPV = Vec<VEC>::kElems;
+  if constexpr (OUT == kOutSame) {
+    uint16_t* o = static_cast<uint16_t*>(a.out) + row * a.out_stride + v * EPV;
+    st_global<VEC>(o, normalize<T, VEC>(rv, wv, inv));
+  } else {
+    uint8_t* o = static_cast<uint8_t*>(a.out) + row * a.out_stride + v * EPV;
+    st_global<VEC / 2>(o, quantize_e4m3<T, VEC>(rv, wv, inv, inv_scale));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 1: one warp per row (rows of at most 4 * 32 vectors).  No shared
 // memory, no block barrier: a warp that has finished its row retires without
 // waiting for the rest of its CTA.
-template <typename T, int VEC, int VPT>
+template <typename T, int VEC, int VPT, bool RES, int OUT>
 __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + (threadIdx.x >> 5);
   pdl_entry();
   if (row >= a.rows) return;
-  uint16_t* xr = a.x + row * a.x_stride;
-  uint16_t* rr = a.r + row * a.r_stride;
+  const uint16_t* xr = a.x + row * a.x_stride;
+  uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
 
@@ -159,7 +263,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
     const int v = lane + 32 * j;
     if (v < a.nvec) {
       xv[j] = ld_stream<VEC>(xr + v * EPV, pol_stream);
-      rv[j] = ld_stream<VEC>(rr + v * EPV, pol_stream);
+      if constexpr (RES) rv[j] = ld_stream<VEC>(rr + v * EPV, pol_stream);
     }
   }
   float a0 = 0.f, a1 = 0.f;
@@ -167,16 +271,30 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   for (int j = 0; j < VPT; ++j) {
     const int v = lane + 32 * j;
     if (v < a.nvec) {
-      add_round<T, VEC>(xv[j], rv[j], a0, a1);
-      st_global<VEC>(rr + v * EPV, xv[j]);
+      if constexpr (RES) {
+        add_round<T, VEC>(xv[j], rv[j], a0, a1);
+        st_global<VEC>(rr + v * EPV, xv[j]);
+      } else {
+        square_sum<T, VEC>(xv[j], a0, a1);
+      }
       wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
     }
   }
   const float inv = rsqrtf(fmaf(warp_sum(a0 + a1), a.inv_hidden, a.eps));
+  float inv_scale = static_inv_scale<OUT>(a);
+  if constexpr (OUT == kOutFp8Dynamic) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+      if (lane + 32 * j < a.nvec) m = vec_amax<T, VEC>(xv[j], wv[j], inv, m);
+    const float scale = fmaxf(warp_max(m), kMinAmax) / kE4m3Max;
+    inv_scale = 1.0f / scale;
+    if (lane == 0) a.row_scales[row] = scale;
+  }
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = lane + 32 * j;
-    if (v < a.nvec) st_global<VEC>(xr + v * EPV, normalize<T, VEC>(xv[j], wv[j], inv));
+    if (v < a.nvec) store_out<T, VEC, OUT>(a, row, v, xv[j], wv[j], inv, inv_scale);
   }
 }
 
@@ -190,18 +308,22 @@ __host__ __device__ constexpr int cta_max_threads(int vpt) {
 // ---------------------------------------------------------------------------
 // Kernel 2: one CTA per row slice; with CLUSTER, the row is split over the
 // CTAs of a thread-block cluster (launched with cluster dims (n, 1, 1)) and
-// the per-CTA partial sums of squares are pushed into every peer's shared
-// memory, so each CTA finishes the reduction locally after one cluster
-// barrier and no CTA touches a peer's memory afterwards.
-template <typename T, int VEC, int VPT, bool CLUSTER>
+// the per-CTA partials (sum of squares, and for dynamic fp8 the amax) are
+// pushed into every peer's shared memory, so each CTA finishes each reduction
+// locally after one cluster barrier and no CTA touches a peer's memory
+// afterwards.
+template <typename T, int VEC, int VPT, bool CLUSTER, bool RES, int OUT>
 __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
   __shared__ float warp_part[32];
+  __shared__ float warp_amax[32];
   __shared__ float cta_part[8];
+  __shared__ float cta_amax[8];
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int nthreads = blockDim.x;
+  const int nwarps = nthreads >> 5;
 
   int64_t row;
   int v_begin = 0, v_end = a.nvec;
@@ -219,8 +341,8 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   } else {
     row = blockIdx.x;
   }
-  uint16_t* xr = a.x + row * a.x_stride;
-  uint16_t* rr = a.r + row * a.r_stride;
+  const uint16_t* xr = a.x + row * a.x_stride;
+  uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
 
@@ -230,7 +352,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
     const int v = v_begin + tid + j * nthreads;
     if (v < v_end) {
       xv[j] = ld_stream<VEC>(xr + static_cast<int64_t>(v) * EPV, pol_stream);
-      rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
+      if constexpr (RES) rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
     }
   }
   float a0 = 0.f, a1 = 0.f;
@@ -238,8 +360,12 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   for (int j = 0; j < VPT; ++j) {
     const int v = v_begin + tid + j * nthreads;
     if (v < v_end) {
-      add_round<T, VEC>(xv[j], rv[j], a0, a1);
-      st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+      if constexpr (RES) {
+        add_round<T, VEC>(xv[j], rv[j], a0, a1);
+        st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+      } else {
+        square_sum<T, VEC>(xv[j], a0, a1);
+      }
       wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
     }
   }
@@ -247,7 +373,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   const float wsum = warp_sum(a0 + a1);
   if (lane == 0) warp_part[warp] = wsum;
   __syncthreads();
-  float total = warp_sum(lane < (nthreads >> 5) ? warp_part[lane] : 0.f);
+  float total = warp_sum(lane < nwarps ? warp_part[lane] : 0.f);
   if constexpr (CLUSTER) {
     cluster_wait();  // phase 1: all peers are running
     if (warp == 0 && lane < static_cast<int>(csize)) st_cluster_f32(&cta_part[crank], lane, total);
@@ -256,23 +382,43 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
     total = warp_sum(lane < static_cast<int>(csize) ? cta_part[lane] : 0.f);
   }
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
+
+  float inv_scale = static_inv_scale<OUT>(a);
+  if constexpr (OUT == kOutFp8Dynamic) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+      if (v_begin + tid + j * nthreads < v_end) m = vec_amax<T, VEC>(xv[j], wv[j], inv, m);
+    m = warp_max(m);
+    if (lane == 0) warp_amax[warp] = m;
+    __syncthreads();
+    float amax = warp_max(lane < nwarps ? warp_amax[lane] : 0.f);
+    if constexpr (CLUSTER) {
+      if (warp == 0 && lane < static_cast<int>(csize)) st_cluster_f32(&cta_amax[crank], lane, amax);
+      cluster_arrive_release();
+      cluster_wait();  // phase 3: every CTA's amax has landed in every CTA
+      amax = warp_max(lane < static_cast<int>(csize) ? cta_amax[lane] : 0.f);
+    }
+    const float scale = fmaxf(amax, kMinAmax) / kE4m3Max;
+    inv_scale = 1.0f / scale;
+    if (crank == 0 && tid == 0) a.row_scales[row] = scale;
+  }
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = v_begin + tid + j * nthreads;
-    if (v < v_end) {
-      st_global<VEC>(xr + static_cast<int64_t>(v) * EPV, normalize<T, VEC>(xv[j], wv[j], inv));
-    }
+    if (v < v_end) store_out<T, VEC, OUT>(a, row, v, xv[j], wv[j], inv, inv_scale);
   }
 }
 
 // ---------------------------------------------------------------------------
-// Kernel 3: rows longer than the register-resident kernels hold.  Pass 1
-// streams input and residual from HBM, writes the rounded residual and sums
-// squares; pass 2 re-reads each thread's own residual vectors from L2 (.cg),
-// multiplies by the weight and writes the output.
+// Kernel 3: rows longer than the register-resident kernels hold (16-bit
+// output only).  Pass 1 streams the input (and residual) from HBM, writes the
+// rounded residual and sums squares; pass 2 re-reads each thread's own
+// residual (or input) vectors from L2 (.cg), multiplies by the weight and
+// writes the output.
 constexpr int kTwoPassThreads = 512;
 
-template <typename T, int VEC>
+template <typename T, int VEC, bool RES>
 __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
   constexpr int U = 4;
@@ -282,8 +428,9 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   const int warp = tid >> 5;
   const int nthreads = blockDim.x;
   const int64_t row = blockIdx.x;
-  uint16_t* xr = a.x + row * a.x_stride;
-  uint16_t* rr = a.r + row * a.r_stride;
+  const uint16_t* xr = a.x + row * a.x_stride;
+  uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
+  uint16_t* orow = static_cast<uint16_t*>(a.out) + row * a.out_stride;
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
   pdl_entry();
@@ -296,15 +443,19 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
       const int v = base + tid + j * nthreads;
       if (v < a.nvec) {
         xv[j] = ld_stream<VEC>(xr + static_cast<int64_t>(v) * EPV, pol_stream);
-        rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
+        if constexpr (RES) rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
       }
     }
 #pragma unroll
     for (int j = 0; j < U; ++j) {
       const int v = base + tid + j * nthreads;
       if (v < a.nvec) {
-        add_round<T, VEC>(xv[j], rv[j], a0, a1);
-        st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+        if constexpr (RES) {
+          add_round<T, VEC>(xv[j], rv[j], a0, a1);
+          st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+        } else {
+          square_sum<T, VEC>(xv[j], a0, a1);
+        }
       }
     }
   }
@@ -314,13 +465,15 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   const float total = warp_sum(lane < (nthreads >> 5) ? warp_part[lane] : 0.f);
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
 
+  // Pass 2 reads the values this thread wrote (residual) or read (input) in pass 1.
+  const uint16_t* src = RES ? rr : xr;
   for (int base = 0; base < a.nvec; base += U * nthreads) {
     Vec<VEC> sv[U], wv[U];
 #pragma unroll
     for (int j = 0; j < U; ++j) {
       const int v = base + tid + j * nthreads;
       if (v < a.nvec) {
-        sv[j] = ld_l2<VEC>(rr + static_cast<int64_t>(v) * EPV);
+        sv[j] = ld_l2<VEC>(src + static_cast<int64_t>(v) * EPV);
         wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
       }
     }
@@ -328,7 +481,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
     for (int j = 0; j < U; ++j) {
       const int v = base + tid + j * nthreads;
       if (v < a.nvec) {
-        st_global<VEC>(xr + static_cast<int64_t>(v) * EPV, normalize<T, VEC>(sv[j], wv[j], inv));
+        st_global<VEC>(orow + static_cast<int64_t>(v) * EPV, normalize<T, VEC>(sv[j], wv[j], inv));
       }
     }
   }
@@ -348,6 +501,15 @@ struct Plan {
   int rows_per_cta = 1;  // warp kind only
 };
 
+// Kernel family of one call: residual or not, and the output form.
+struct Variant {
+  bool res = true;
+  int out = kOutSame;
+  // The in-place fused form (the reference's operation) carries the full set
+  // of compiled plans; the other forms a reduced set.
+  bool full() const { return res && out == kOutSame; }
+};
+
 const char* kind_name(Kind k) {
   switch (k) {
     case kWarpRows: return "warp";
@@ -364,8 +526,17 @@ std::string plan_string(const Plan& p) {
   return buf;
 }
 
-// VPT values compiled for each kind (must match the dispatch tables below).
-bool vpt_supported(Kind k, int vec, int vpt) {
+// VPT values compiled for each kind and variant (must match the dispatch
+// tables below).
+bool vpt_supported(Kind k, int vec, int vpt, const Variant& v) {
+  if (!v.full()) {
+    switch (k) {
+      case kWarpRows: return vpt == 1 || vpt == 2 || vpt == 4;
+      case kCtaRows: return vpt == 1 || vpt == 2 || vpt == 4;
+      case kClusterRows: return vpt == 2 || vpt == 4;
+      default: return v.out == kOutSame;
+    }
+  }
   switch (k) {
     case kWarpRows: return vpt >= 1 && vpt <= 4;
     case kCtaRows:
@@ -378,25 +549,6 @@ bool vpt_supported(Kind k, int vec, int vpt) {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-int next_supported_vpt(Kind k, int vec, int vpt) {
-  for (int v = vpt; v <= 8; ++v)
-    if (vpt_supported(k, vec, v)) return v;
-  return -1;
-}
-
-// Largest vector width every pointer, stride and the hidden size allow.
-int choose_vec(int64_t hidden, int64_t rows, const void* x, const void* r, const void* w,
-               int64_t xs, int64_t rs) {
-  for (int vec : {32, 16, 8, 4}) {
-    const int epv = vec / 2;
-    if (hidden % epv) continue;
-    if (!aligned(x, vec) || !aligned(r, vec) || !aligned(w, vec)) continue;
-    if (rows > 1 && (((xs * 2) % vec) || ((rs * 2) % vec))) continue;
-    return vec;
-  }
-  return 2;
-}
-
 // Launch-plan heuristic, fitted to a cold-L2 sweep of every compiled plan on
 // B200 (batch 4096 bf16, hidden 1024..32768; the kernel timed as back-to-back
 // CUDA-graph launches over rotating buffers).  What won everywhere:
@@ -408,9 +560,9 @@ int choose_vec(int64_t hidden, int64_t rows, const void* x, const void* r, const
 //     vectors, where 1024-thread CTAs would leave SMs a CTA short);
 //   * thread-block clusters only once a row no longer fits one CTA: splitting
 //     rows that do fit cost 5-15% (cluster scheduling and the cluster barrier).
-Plan default_plan(int64_t rows, int nvec, int vec, const DeviceInfo& dev) {
-  (void)rows;
-  (void)dev;
+// Every plan it returns is compiled for every variant, except two passes
+// (rows past 8 * 2048 vectors), which only the 16-bit-output variants have.
+Plan default_plan(int nvec, int vec) {
   Plan p;
   p.vec = vec;
   if (nvec <= 64) {
@@ -476,13 +628,13 @@ bool parse_plan(const std::string& s, Plan* p) {
 }
 
 // Checks that `p` covers a row of `nvec` vectors within hardware limits.
-bool plan_valid(const Plan& p, int nvec, int max_vec, std::string* why) {
+bool plan_valid(const Plan& p, int nvec, int max_vec, const Variant& var, std::string* why) {
   if (p.vec > max_vec || (p.vec != 32 && p.vec != 16 && p.vec != 8 && p.vec != 4 && p.vec != 2)) {
     *why = "vector width not allowed by alignment / hidden size";
     return false;
   }
-  if (!vpt_supported(p.kind, p.vec, p.vpt)) {
-    *why = "vectors-per-thread value not compiled for this kernel";
+  if (!vpt_supported(p.kind, p.vec, p.vpt, var)) {
+    *why = "vectors-per-thread value (or kernel kind) not compiled for this variant";
     return false;
   }
   switch (p.kind) {
@@ -520,134 +672,234 @@ bool plan_valid(const Plan& p, int nvec, int max_vec, std::string* why) {
 }
 
 // ---------------------------------------------------------------------------
-// Dispatch: (dtype, vec, kind, vpt) -> kernel function pointer.
+// Dispatch: (dtype, variant, vec, kind, vpt) -> kernel function pointer.
 
 using KernelFn = void (*)(RmsArgs);
 
-template <typename T, int VEC>
+template <typename T, int VEC, bool RES, int OUT>
 KernelFn pick_warp(int vpt) {
+  if constexpr (RES && OUT == kOutSame) {
+    if (vpt == 3) return rms_norm_warp_rows<T, VEC, 3, RES, OUT>;
+  }
   switch (vpt) {
-    case 1: return rms_norm_warp_rows<T, VEC, 1>;
-    case 2: return rms_norm_warp_rows<T, VEC, 2>;
-    case 3: return rms_norm_warp_rows<T, VEC, 3>;
-    case 4: return rms_norm_warp_rows<T, VEC, 4>;
+    case 1: return rms_norm_warp_rows<T, VEC, 1, RES, OUT>;
+    case 2: return rms_norm_warp_rows<T, VEC, 2, RES, OUT>;
+    case 4: return rms_norm_warp_rows<T, VEC, 4, RES, OUT>;
   }
   return nullptr;
 }
 
-template <typename T, int VEC, bool CL>
+template <typename T, int VEC, bool CL, bool RES, int OUT>
 KernelFn pick_cta(int vpt) {
-  if constexpr (VEC == 32) {
-    switch (vpt) {
-      case 3: return rms_norm_cta_rows<T, VEC, 3, CL>;
-      case 6: return rms_norm_cta_rows<T, VEC, 6, CL>;
+  if constexpr (RES && OUT == kOutSame) {
+    if constexpr (VEC == 32) {
+      switch (vpt) {
+        case 3: return rms_norm_cta_rows<T, VEC, 3, CL, RES, OUT>;
+        case 6: return rms_norm_cta_rows<T, VEC, 6, CL, RES, OUT>;
+      }
     }
+    if (vpt == 8) return rms_norm_cta_rows<T, VEC, 8, CL, RES, OUT>;
   }
   switch (vpt) {
-    case 1: return rms_norm_cta_rows<T, VEC, 1, CL>;
-    case 2: return rms_norm_cta_rows<T, VEC, 2, CL>;
-    case 4: return rms_norm_cta_rows<T, VEC, 4, CL>;
-    case 8: return rms_norm_cta_rows<T, VEC, 8, CL>;
+    case 1:
+      if constexpr (!CL || (RES && OUT == kOutSame)) return rms_norm_cta_rows<T, VEC, 1, CL, RES, OUT>;
+      return nullptr;
+    case 2: return rms_norm_cta_rows<T, VEC, 2, CL, RES, OUT>;
+    case 4: return rms_norm_cta_rows<T, VEC, 4, CL, RES, OUT>;
   }
   return nullptr;
 }
 
-template <typename T, int VEC>
+template <typename T, int VEC, bool RES, int OUT>
 KernelFn pick_kind(const Plan& p) {
   switch (p.kind) {
-    case kWarpRows: return pick_warp<T, VEC>(p.vpt);
-    case kCtaRows: return pick_cta<T, VEC, false>(p.vpt);
-    case kClusterRows: return pick_cta<T, VEC, true>(p.vpt);
-    default: return rms_norm_two_pass<T, VEC>;
+    case kWarpRows: return pick_warp<T, VEC, RES, OUT>(p.vpt);
+    case kCtaRows: return pick_cta<T, VEC, false, RES, OUT>(p.vpt);
+    case kClusterRows: return pick_cta<T, VEC, true, RES, OUT>(p.vpt);
+    default:
+      if constexpr (OUT == kOutSame) return rms_norm_two_pass<T, VEC, RES>;
+      return nullptr;
+  }
+}
+
+template <typename T, bool RES, int OUT>
+KernelFn pick_vec(const Plan& p) {
+  if constexpr (OUT == kOutSame) {
+    switch (p.vec) {
+      case 32: return pick_kind<T, 32, RES, OUT>(p);
+      case 16: return pick_kind<T, 16, RES, OUT>(p);
+      case 8: return pick_kind<T, 8, RES, OUT>(p);
+      case 4: return pick_kind<T, 4, RES, OUT>(p);
+      default: return pick_kind<T, 2, RES, OUT>(p);
+    }
+  } else {
+    switch (p.vec) {
+      case 32: return pick_kind<T, 32, RES, OUT>(p);
+      case 16: return pick_kind<T, 16, RES, OUT>(p);
+      case 8: return pick_kind<T, 8, RES, OUT>(p);
+      default: return nullptr;  // fp8 output needs >= 4 elements per vector
+    }
   }
 }
 
 template <typename T>
-KernelFn pick_vec(const Plan& p) {
-  switch (p.vec) {
-    case 32: return pick_kind<T, 32>(p);
-    case 16: return pick_kind<T, 16>(p);
-    case 8: return pick_kind<T, 8>(p);
-    case 4: return pick_kind<T, 4>(p);
-    default: return pick_kind<T, 2>(p);
+KernelFn pick_variant(const Plan& p, const Variant& v) {
+  if (v.res) {
+    switch (v.out) {
+      case kOutSame: return pick_vec<T, true, kOutSame>(p);
+      case kOutFp8Static: return pick_vec<T, true, kOutFp8Static>(p);
+      default: return pick_vec<T, true, kOutFp8Dynamic>(p);
+    }
+  }
+  switch (v.out) {
+    case kOutSame: return pick_vec<T, false, kOutSame>(p);
+    case kOutFp8Static: return pick_vec<T, false, kOutFp8Static>(p);
+    default: return pick_vec<T, false, kOutFp8Dynamic>(p);
   }
 }
 
-KernelFn pick_kernel(int dtype, const Plan& p) {
-  return dtype == HPRN_DTYPE_BF16 ? pick_vec<__nv_bfloat16>(p) : pick_vec<__half>(p);
+KernelFn pick_kernel(int dtype, const Plan& p, const Variant& v) {
+  return dtype == HPRN_DTYPE_BF16 ? pick_variant<__nv_bfloat16>(p, v)
+                                  : pick_variant<__half>(p, v);
 }
 
 // Max CTAs per launch in grid.x (2^31 - 1), kept a multiple of 8 for clusters.
 constexpr int64_t kMaxGridX = 2147483640LL;
 
 struct Problem {
-  void* x;
+  void* out;
+  const void* x;
   const void* w;
-  void* r;
-  int64_t rows, hidden, xs, rs;
+  void* r;  // null: plain RMSNorm
+  int64_t rows, hidden, os, xs, rs;
   double eps;
   int dtype;
+  int out_form;
+  const float* scale;
+  float* row_scales;
 };
+
+int out_elem_bytes(const Problem& q) { return q.out_form == kOutSame ? 2 : 1; }
+
+// [first, last) byte range of `rows` rows of `hidden` elements at `stride`.
+struct Span {
+  const char* b;
+  const char* e;
+};
+
+Span span_of(const void* p, int64_t rows, int64_t hidden, int64_t stride, int elem) {
+  const char* b = static_cast<const char*>(p);
+  return {b, b + elem * ((rows - 1) * stride + hidden)};
+}
+
+bool overlap(const Span& a, const Span& b) { return a.b < b.e && b.b < a.e; }
+
+// Two strided 16-bit row sets that overlap as ranges can still share no
+// element when their rows interleave (same stride, offset between rows).
+bool rows_interleave(const void* p, const void* q, int64_t stride_p, int64_t stride_q,
+                     int64_t hidden) {
+  const char* a = static_cast<const char*>(p);
+  const char* b = static_cast<const char*>(q);
+  if (stride_p != stride_q || (b - a) % 2) return false;
+  const int64_t d = (b - a) / 2;
+  const int64_t m = ((d % stride_p) + stride_p) % stride_p;
+  return m >= hidden && stride_p - m >= hidden;
+}
 
 int validate(const Problem& q) {
   if (q.dtype != HPRN_DTYPE_BF16 && q.dtype != HPRN_DTYPE_FP16)
     return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
+  if (q.out_form != kOutSame && q.out_form != kOutFp8Static && q.out_form != kOutFp8Dynamic)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown output form");
   if (q.rows < 0) return fail(HPRN_ERR_INVALID_ARGUMENT, "rows must be >= 0");
   if (q.hidden < 1 || q.hidden > (static_cast<int64_t>(1) << 30))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "hidden_dim must be in [1, 2^30]");
   if (q.rows == 0) return HPRN_OK;
-  if (!q.x || !q.w || !q.r) return fail(HPRN_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (!aligned(q.x, 2) || !aligned(q.w, 2) || !aligned(q.r, 2))
+  if (!q.x || !q.w || !q.out) return fail(HPRN_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (q.out_form == kOutFp8Static && !q.scale)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "static fp8 output needs a scale");
+  if (q.out_form == kOutFp8Dynamic && !q.row_scales)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "dynamic fp8 output needs a row_scales buffer");
+  if (!aligned(q.x, 2) || !aligned(q.w, 2) || (q.r && !aligned(q.r, 2)) ||
+      (q.out_form == kOutSame && !aligned(q.out, 2)))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor pointers must be 2-byte aligned");
-  if (q.rows > 1 && (q.xs < q.hidden || q.rs < q.hidden))
+  if (q.rows > 1 && (q.xs < q.hidden || q.os < q.hidden || (q.r && q.rs < q.hidden)))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "row strides must be >= hidden_dim");
+  const Span xs = span_of(q.x, q.rows, q.hidden, q.xs, 2);
+  const Span ws = span_of(q.w, 1, q.hidden, q.hidden, 2);
+  const Span os = span_of(q.out, q.rows, q.hidden, q.os, out_elem_bytes(q));
   // input and residual must not share any element.
-  const int64_t xspan = (q.rows - 1) * q.xs + q.hidden;
-  const int64_t rspan = (q.rows - 1) * q.rs + q.hidden;
-  const char* xb = static_cast<const char*>(q.x);
-  const char* rb = static_cast<const char*>(q.r);
-  const bool spans_overlap = xb < rb + 2 * rspan && rb < xb + 2 * xspan;
-  if (spans_overlap) {
-    bool disjoint_rows = false;
-    const int64_t d = (rb - xb) / 2;
-    if (q.xs == q.rs && (rb - xb) % 2 == 0) {
-      const int64_t m = ((d % q.xs) + q.xs) % q.xs;
-      disjoint_rows = m >= q.hidden && q.xs - m >= q.hidden;
-    }
-    if (!disjoint_rows) return fail(HPRN_ERR_INVALID_ARGUMENT, "input and residual must not overlap");
+  if (q.r) {
+    const Span rs = span_of(q.r, q.rows, q.hidden, q.rs, 2);
+    if (overlap(xs, rs) && !rows_interleave(q.x, q.r, q.xs, q.rs, q.hidden))
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "input and residual must not overlap");
+    if (overlap(os, rs) && !(q.out_form == kOutSame && rows_interleave(q.out, q.r, q.os, q.rs, q.hidden)))
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "output and residual must not overlap");
+    if (overlap(ws, rs)) return fail(HPRN_ERR_INVALID_ARGUMENT, "weight must not overlap input or residual");
   }
-  // The weight is read through the non-coherent cache: it must not be written by this call.
-  const char* wb = static_cast<const char*>(q.w);
-  if ((wb < xb + 2 * xspan && xb < wb + 2 * q.hidden) || (wb < rb + 2 * rspan && rb < wb + 2 * q.hidden))
+  // The output is either exactly the input (16-bit, same strides: in place) or disjoint from it.
+  const bool in_place = q.out_form == kOutSame && q.out == q.x && (q.os == q.xs || q.rows == 1);
+  if (!in_place && overlap(os, xs) &&
+      !(q.out_form == kOutSame && rows_interleave(q.out, q.x, q.os, q.xs, q.hidden)))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "output must be the input itself or not overlap it");
+  // The weight is read through the non-coherent cache: nothing this call writes may alias it.
+  if (overlap(ws, os))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "weight must not overlap input or residual");
   return HPRN_OK;
 }
 
-int make_plan(const Problem& q, const DeviceInfo& dev, Plan* plan, RmsArgs* args) {
-  const int max_vec = choose_vec(q.hidden, q.rows, q.x, q.r, q.w, q.xs, q.rs);
+// Largest vector width every pointer, stride and the hidden size allow.
+int choose_vec(const Problem& q) {
+  const bool fp8 = q.out_form != kOutSame;
+  for (int vec : {32, 16, 8, 4}) {
+    const int epv = vec / 2;
+    if (q.hidden % epv) continue;
+    if (!aligned(q.x, vec) || !aligned(q.w, vec) || (q.r && !aligned(q.r, vec))) continue;
+    const int out_vec = fp8 ? vec / 2 : vec;
+    if (!aligned(q.out, out_vec)) continue;
+    if (q.rows > 1 && (((q.xs * 2) % vec) || (q.r && (q.rs * 2) % vec) ||
+                       ((q.os * (fp8 ? 1 : 2)) % out_vec)))
+      continue;
+    return vec;
+  }
+  return 2;
+}
+
+int make_plan(const Problem& q, Plan* plan, RmsArgs* args) {
+  const Variant var{q.r != nullptr, q.out_form};
+  const int max_vec = choose_vec(q);
+  if (q.out_form != kOutSame && max_vec < 8)
+    return fail(HPRN_ERR_INVALID_ARGUMENT,
+                "fp8 output needs hidden_dim % 4 == 0 and 8-byte aligned input/weight/residual "
+                "rows and 4-byte aligned output rows");
   const int nvec = static_cast<int>(q.hidden / (max_vec / 2));
-  Plan p = default_plan(q.rows, nvec, max_vec, dev);
+  Plan p = default_plan(nvec, max_vec);
+  if (p.kind == kTwoPass && q.out_form != kOutSame)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "rows longer than 16384 vectors are supported with a "
+                                           "16-bit output only");
   if (g_override_set) {
     Plan o;
     std::string why;
     if (!parse_plan(g_override, &o)) return fail(HPRN_ERR_INVALID_ARGUMENT, "unparsable plan override");
-    const int onvec = static_cast<int>(q.hidden / (o.vec / 2));
-    if (o.vec <= max_vec && q.hidden % (o.vec / 2) == 0 && plan_valid(o, onvec, max_vec, &why)) {
-      p = o;
-    } else if (o.vec <= max_vec && q.hidden % (o.vec / 2) == 0) {
-      return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override rejected: " + why);
-    } else {
+    if (o.vec > max_vec || q.hidden % (o.vec / 2) != 0)
       return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override vector width not allowed here");
-    }
+    const int onvec = static_cast<int>(q.hidden / (o.vec / 2));
+    if (!plan_valid(o, onvec, max_vec, var, &why))
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override rejected: " + why);
+    p = o;
   }
   const int epv = p.vec / 2;
   RmsArgs a;
-  a.x = static_cast<uint16_t*>(q.x);
+  a.x = static_cast<const uint16_t*>(q.x);
   a.w = static_cast<const uint16_t*>(q.w);
   a.r = static_cast<uint16_t*>(q.r);
+  a.out = q.out;
+  a.scale = q.scale;
+  a.row_scales = q.row_scales;
   a.rows = q.rows;
   a.x_stride = q.xs;
   a.r_stride = q.rs;
+  a.out_stride = q.os;
   a.nvec = static_cast<int>(q.hidden / epv);
   a.slice_vecs = (a.nvec + p.cluster - 1) / p.cluster;
   a.rows_per_cta = p.rows_per_cta;
@@ -658,19 +910,23 @@ int make_plan(const Problem& q, const DeviceInfo& dev, Plan* plan, RmsArgs* args
   return HPRN_OK;
 }
 
-int launch(const Plan& p, RmsArgs a, int dtype, cudaStream_t stream, unsigned flags) {
-  KernelFn fn = pick_kernel(dtype, p);
+int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, cudaStream_t stream,
+           unsigned flags) {
+  KernelFn fn = pick_kernel(dtype, p, var);
   if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
   // Rows handled per CTA-group in grid.x; split very tall problems into launches.
   const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;
   const int64_t ctas_per_unit = p.kind == kClusterRows ? p.cluster : 1;
   const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
+  const int out_bytes = var.out == kOutSame ? 2 : 1;
   int64_t done = 0;
   while (done < a.rows) {
     RmsArgs c = a;
     const int64_t n = a.rows - done < max_rows ? a.rows - done : max_rows;
     c.x = a.x + done * a.x_stride;
-    c.r = a.r + done * a.r_stride;
+    if (a.r) c.r = a.r + done * a.r_stride;
+    c.out = static_cast<char*>(a.out) + done * a.out_stride * out_bytes;
+    if (a.row_scales) c.row_scales = a.row_scales + done;
     c.rows = n;
     const int64_t units = (n + rows_per_unit - 1) / rows_per_unit;
     cudaLaunchConfig_t cfg = {};
@@ -702,6 +958,23 @@ int launch(const Plan& p, RmsArgs a, int dtype, cudaStream_t stream, unsigned fl
   return HPRN_OK;
 }
 
+int run(const Problem& q, void* stream, unsigned flags) {
+  if (flags & ~static_cast<unsigned>(HPRN_LAUNCH_PDL))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown launch flags");
+  int st = validate(q);
+  if (st != HPRN_OK) return st;
+  if (q.rows == 0) return ok();
+  const DeviceInfo* dev = nullptr;
+  if ((st = current_device(&dev)) != HPRN_OK) return st;
+  Plan p;
+  RmsArgs a;
+  if ((st = make_plan(q, &p, &a)) != HPRN_OK) return st;
+  const Variant var{q.r != nullptr, q.out_form};
+  if ((st = launch(p, a, q.dtype, var, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK)
+    return st;
+  return ok();
+}
+
 }  // namespace hprn
 
 extern "C" {
@@ -717,19 +990,22 @@ int hprn_rms_norm_ex(void* input, const void* weight, void* residual, int64_t ro
                      int64_t hidden, int64_t input_row_stride, int64_t residual_row_stride,
                      double eps, int dtype, void* stream, unsigned flags) {
   using namespace hprn;
-  if (flags & ~static_cast<unsigned>(HPRN_LAUNCH_PDL))
-    return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown launch flags");
-  Problem q{input, weight, residual, rows, hidden, input_row_stride, residual_row_stride, eps, dtype};
-  int st = validate(q);
-  if (st != HPRN_OK) return st;
-  if (rows == 0) return ok();
-  const DeviceInfo* dev = nullptr;
-  if ((st = current_device(&dev)) != HPRN_OK) return st;
-  Plan p;
-  RmsArgs a;
-  if ((st = make_plan(q, *dev, &p, &a)) != HPRN_OK) return st;
-  if ((st = launch(p, a, dtype, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK) return st;
-  return ok();
+  if (!residual && rows > 0)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "null tensor pointer (residual)");
+  Problem q{input, input, weight, residual, rows, hidden, input_row_stride, input_row_stride,
+            residual_row_stride, eps, dtype, kOutSame, nullptr, nullptr};
+  return run(q, stream, flags);
+}
+
+int hprn_rms_norm_out(void* out, const void* input, const void* weight, void* residual,
+                      int64_t rows, int64_t hidden, int64_t out_row_stride,
+                      int64_t input_row_stride, int64_t residual_row_stride, double eps,
+                      int dtype, int out_form, const float* scale, float* row_scales,
+                      void* stream, unsigned flags) {
+  using namespace hprn;
+  Problem q{out, input, weight, residual, rows, hidden, out_row_stride, input_row_stride,
+            residual_row_stride, eps, dtype, out_form, scale, row_scales};
+  return run(q, stream, flags);
 }
 
 int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* input,
@@ -741,21 +1017,15 @@ int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* inpu
     return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
   if (hidden < 1 || hidden > (static_cast<int64_t>(1) << 30))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "hidden_dim must be in [1, 2^30]");
-  // The weight's alignment is assumed to match the input's for planning.
-  Problem q{const_cast<void*>(input), input, const_cast<void*>(residual), rows < 1 ? 1 : rows,
-            hidden, input_row_stride, residual_row_stride, 1e-6, dtype};
-  int st;
-  const DeviceInfo* dev = nullptr;
-  DeviceInfo fake;
-  if (current_device(&dev) != HPRN_OK) {
-    // No usable device: plan for a 148-SM B200 so the heuristic can be inspected offline.
-    fake.sm_count = 148;
-    fake.cc_major = 10;
-    dev = &fake;
-  }
+  // In-place fused form; the weight's alignment is assumed to match the input's.
+  void* x = const_cast<void*>(input);
+  Problem q{x, input, input, const_cast<void*>(residual), rows < 1 ? 1 : rows, hidden,
+            input_row_stride, input_row_stride, residual_row_stride, 1e-6, dtype, kOutSame,
+            nullptr, nullptr};
   Plan p;
   RmsArgs a;
-  if ((st = make_plan(q, *dev, &p, &a)) != HPRN_OK) return st;
+  const int st = make_plan(q, &p, &a);
+  if (st != HPRN_OK) return st;
   snprintf(plan, plan_len, "%s", plan_string(p).c_str());
   return ok();
 }

@@ -124,24 +124,126 @@ void relu(at::Tensor& out, const at::Tensor& input) {
   check_status(hprn_relu(out.data_ptr(), input.data_ptr(), rows, hidden, os, is, dtype, stream));
 }
 
+// Common checks of the out-of-place forms (extensions past the reference).
+struct OutCall {
+  int64_t rows = 0, hidden = 0, os = 0, xs = 0, rs = 0;
+  int dtype = 0;
+};
+
+OutCall check_out_call(const at::Tensor& out, const at::Tensor& input, const at::Tensor& weight,
+                       const c10::optional<at::Tensor>& residual) {
+  OutCall c;
+  TORCH_CHECK(input.dim() >= 1, "input.dim() >= 1");
+  TORCH_CHECK(weight.dim() == 1, "weight.dim() == 1");
+  c.hidden = weight.size(0);
+  TORCH_CHECK(input.size(-1) == c.hidden, "input.size(-1) == hidden_dim");
+  TORCH_CHECK(out.sizes() == input.sizes(), "out must have the input's shape");
+  TORCH_CHECK(input.is_cuda() && weight.is_cuda() && out.is_cuda(), "tensors must be CUDA tensors");
+  TORCH_CHECK(weight.device() == input.device() && out.device() == input.device(),
+              "tensors must be on the same device");
+  TORCH_CHECK(weight.scalar_type() == input.scalar_type(), "input and weight must have the same dtype");
+  TORCH_CHECK(c.hidden <= 1 || weight.stride(0) == 1, "weight must be contiguous");
+  TORCH_CHECK(input.stride(-1) == 1 || c.hidden == 1, "input.stride(-1) == 1");
+  TORCH_CHECK(out.stride(-1) == 1 || c.hidden == 1, "out.stride(-1) == 1");
+  c.dtype = dtype_code(input);
+  rows_of(input, "input", &c.rows, &c.xs);
+  int64_t orows = 0;
+  rows_of(out, "out", &orows, &c.os);
+  c.rs = c.hidden;
+  if (residual.has_value()) {
+    const at::Tensor& r = *residual;
+    TORCH_CHECK(r.sizes() == input.sizes(), "residual must have the input's shape");
+    TORCH_CHECK(r.is_cuda() && r.device() == input.device(), "residual must be on the input's device");
+    TORCH_CHECK(r.scalar_type() == input.scalar_type(), "input and residual must have the same dtype");
+    TORCH_CHECK(r.stride(-1) == 1 || c.hidden == 1, "residual.stride(-1) == 1");
+    int64_t rrows = 0;
+    rows_of(r, "residual", &rrows, &c.rs);
+  }
+  return c;
+}
+
+// out <- RMSNorm(input [+ residual]) * weight in the input's dtype; the
+// residual (if given) is updated in place; out may be the input itself.
+void rms_norm_out(at::Tensor& out, const at::Tensor& input, const at::Tensor& weight,
+                  c10::optional<at::Tensor> residual, double eps) {
+  TORCH_CHECK(out.scalar_type() == input.scalar_type(), "out must have the input's dtype");
+  const OutCall c = check_out_call(out, input, weight, residual);
+  if (c.rows == 0 || c.hidden == 0) return;
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_rms_norm_out(out.data_ptr(), input.data_ptr(), weight.data_ptr(),
+                                 residual.has_value() ? residual->data_ptr() : nullptr, c.rows,
+                                 c.hidden, c.os, c.xs, c.rs, eps, c.dtype, HPRN_OUT_SAME, nullptr,
+                                 nullptr, stream, HPRN_LAUNCH_DEFAULT));
+}
+
+// out (float8_e4m3fn) <- e4m3(RMSNorm(input [+ residual]) * weight / scale):
+// with `scale` (one float32) a static per-tensor scale, with `row_scales`
+// (float32 [rows], written) a per-row scale max|y| / 448.
+void rms_norm_fp8(at::Tensor& out, const at::Tensor& input, const at::Tensor& weight,
+                  c10::optional<at::Tensor> residual, double eps, c10::optional<at::Tensor> scale,
+                  c10::optional<at::Tensor> row_scales) {
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn, "out must be float8_e4m3fn");
+  TORCH_CHECK(scale.has_value() != row_scales.has_value(),
+              "exactly one of scale (static) and row_scales (dynamic) must be given");
+  const OutCall c = check_out_call(out, input, weight, residual);
+  const float* sp = nullptr;
+  float* rsp = nullptr;
+  if (scale.has_value()) {
+    TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->numel() == 1 && scale->is_cuda() &&
+                    scale->device() == input.device(),
+                "scale must be one float32 on the input's device");
+    sp = scale->data_ptr<float>();
+  } else {
+    TORCH_CHECK(row_scales->scalar_type() == at::kFloat && row_scales->numel() == c.rows &&
+                    row_scales->is_contiguous() && row_scales->is_cuda() &&
+                    row_scales->device() == input.device(),
+                "row_scales must be a contiguous float32 tensor with one entry per row");
+    rsp = row_scales->data_ptr<float>();
+  }
+  if (c.rows == 0 || c.hidden == 0) return;
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_rms_norm_out(out.data_ptr(), input.data_ptr(), weight.data_ptr(),
+                                 residual.has_value() ? residual->data_ptr() : nullptr, c.rows,
+                                 c.hidden, c.os, c.xs, c.rs, eps, c.dtype,
+                                 sp ? HPRN_OUT_FP8_E4M3_STATIC : HPRN_OUT_FP8_E4M3_DYNAMIC, sp,
+                                 rsp, stream, HPRN_LAUNCH_DEFAULT));
+}
+
 // Shape-only kernels for tracing (torch.compile / FakeTensor): the ops return
 // nothing and only mutate their annotated arguments.
 void rms_norm_meta(at::Tensor&, const at::Tensor&, at::Tensor&, double) {}
 void relu_meta(at::Tensor&, const at::Tensor&) {}
+void rms_norm_out_meta(at::Tensor&, const at::Tensor&, const at::Tensor&,
+                       c10::optional<at::Tensor>, double) {}
+void rms_norm_fp8_meta(at::Tensor&, const at::Tensor&, const at::Tensor&,
+                       c10::optional<at::Tensor>, double, c10::optional<at::Tensor>,
+                       c10::optional<at::Tensor>) {}
 
 }  // namespace
 
 TORCH_LIBRARY(hp_rms_norm, m) {
+  // The reference's two operators.
   m.def("rms_norm(Tensor(a!) input, Tensor weight, Tensor(b!) residual, float eps) -> ()");
   m.def("relu(Tensor(a!) out, Tensor input) -> ()");
+  // Extensions: plain / out-of-place RMSNorm and fp8-output RMSNorm.
+  m.def("rms_norm_out(Tensor(a!) out, Tensor input, Tensor weight, Tensor(b!)? residual, "
+        "float eps) -> ()");
+  m.def("rms_norm_fp8(Tensor(a!) out, Tensor input, Tensor weight, Tensor(b!)? residual, "
+        "float eps, Tensor? scale, Tensor(c!)? row_scales) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(hp_rms_norm, CUDA, m) {
   m.impl("rms_norm", &rms_norm);
   m.impl("relu", &relu);
+  m.impl("rms_norm_out", &rms_norm_out);
+  m.impl("rms_norm_fp8", &rms_norm_fp8);
 }
 
 TORCH_LIBRARY_IMPL(hp_rms_norm, Meta, m) {
   m.impl("rms_norm", &rms_norm_meta);
   m.impl("relu", &relu_meta);
+  m.impl("rms_norm_out", &rms_norm_out_meta);
+  m.impl("rms_norm_fp8", &rms_norm_fp8_meta);
 }

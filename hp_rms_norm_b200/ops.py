@@ -1,10 +1,16 @@
-"""Python API, argument for argument the reference's (hp_rms_norm/ops.py:4-24).
+"""Python API.
 
+The reference's two functions, argument for argument (hp_rms_norm/ops.py:4-24):
 ``hp_rms_norm(input, weight, residual, eps)`` runs the fused residual add +
 RMSNorm in place (``residual += input``; ``input = RMSNorm(residual) * weight``)
 and returns None; ``relu(output, input)`` writes ``torch.relu(input)`` into
-``output`` and returns None.  Both dispatch through ``torch.ops.hp_rms_norm``,
-which this package registers from its compiled ``_C`` extension.
+``output`` and returns None.
+
+Extensions (not in the reference): ``rms_norm`` (plain RMSNorm),
+``fused_add_rms_norm`` (the fused op into a separate output) and
+``rms_norm_fp8`` (either form with an fp8 e4m3 output, static or per-row
+scale).  Everything dispatches through ``torch.ops.hp_rms_norm``, registered
+by this package's compiled ``_C`` extension.
 """
 import torch
 
@@ -25,4 +31,38 @@ def relu(
     torch.ops.hp_rms_norm.relu.default(output, input)
 
 
-__all__ = ["hp_rms_norm", "relu", "torch"]
+def rms_norm(input, weight, eps, out=None):
+    """RMSNorm without a residual: out = input * rsqrt(mean(input^2) + eps) * weight,
+    in the input's dtype; ``out`` may be ``input`` (in place).  Returns ``out``."""
+    if out is None:
+        out = torch.empty_like(input)
+    torch.ops.hp_rms_norm.rms_norm_out.default(out, input, weight, None, eps)
+    return out
+
+
+def fused_add_rms_norm(input, residual, weight, eps, out=None):
+    """``hp_rms_norm`` into a separate output: residual += input (in place);
+    out = RMSNorm(residual) * weight; ``input`` is left unchanged unless it is
+    ``out``.  Returns ``out``."""
+    if out is None:
+        out = torch.empty_like(input)
+    torch.ops.hp_rms_norm.rms_norm_out.default(out, input, weight, residual, eps)
+    return out
+
+
+def rms_norm_fp8(input, weight, eps, residual=None, scale=None, out=None):
+    """RMSNorm (fused with ``residual += input`` when a residual is given) with
+    an fp8 e4m3 output.  With ``scale`` (a one-element float32 tensor) the output
+    is e4m3(y / scale); without it, each row gets scale max|y| / 448, returned
+    as a float32 tensor of shape input.shape[:-1].  Returns (out, scales)."""
+    if out is None:
+        out = torch.empty(input.shape, dtype=torch.float8_e4m3fn, device=input.device)
+    if scale is not None:
+        torch.ops.hp_rms_norm.rms_norm_fp8.default(out, input, weight, residual, eps, scale, None)
+        return out, scale
+    row_scales = torch.empty(input.shape[:-1], dtype=torch.float32, device=input.device)
+    torch.ops.hp_rms_norm.rms_norm_fp8.default(out, input, weight, residual, eps, None, row_scales)
+    return out, row_scales
+
+
+__all__ = ["hp_rms_norm", "relu", "rms_norm", "fused_add_rms_norm", "rms_norm_fp8", "torch"]

@@ -52,6 +52,13 @@ typedef enum hprn_dtype {
 #define HPRN_LAUNCH_PDL 1u
 #define HPRN_LAUNCH_DEFAULT HPRN_LAUNCH_PDL
 
+/* Output forms of hprn_rms_norm_out. */
+typedef enum hprn_out_form {
+  HPRN_OUT_SAME = 0,              /* 16-bit, the input's dtype */
+  HPRN_OUT_FP8_E4M3_STATIC = 1,   /* fp8 e4m3 (OCP E4M3FN), one scale for the tensor */
+  HPRN_OUT_FP8_E4M3_DYNAMIC = 2   /* fp8 e4m3, one scale per row, written to row_scales */
+} hprn_out_form;
+
 typedef enum hprn_status {
   HPRN_OK = 0,
   HPRN_ERR_INVALID_ARGUMENT = -1, /* bad size, stride, null pointer, overlap */
@@ -112,6 +119,32 @@ HPRN_API int hprn_rms_norm_ex(void* input, const void* weight, void* residual, i
 HPRN_API int hprn_relu_ex(void* out, const void* input, int64_t rows, int64_t hidden,
                           int64_t out_row_stride, int64_t input_row_stride, int dtype,
                           void* stream, unsigned flags);
+
+/*
+ * RMSNorm with or without the residual add, into a separate output, 16-bit or
+ * fp8 (an extension past the reference, whose only form is hprn_rms_norm's):
+ *
+ *   residual == NULL (plain RMSNorm):  s_j = f32(input[i, j])
+ *   residual != NULL (fused add):      s_j = f32(input[i, j]) + f32(residual[i, j]),
+ *                                      residual[i, j] <- round_T(s_j)  (in place)
+ *   inv_i = rsqrt(eps + sum_j s_j^2 / hidden)
+ *   y_ij  = v_ij * f32(weight[j]) * inv_i, v_ij the rounded residual (fused) or f32(input)
+ *   HPRN_OUT_SAME:             out[i, j] = round_T(y_ij)      (out may be `input` itself)
+ *   HPRN_OUT_FP8_E4M3_STATIC:  out[i, j] = e4m3(y_ij * (1 / *scale))
+ *   HPRN_OUT_FP8_E4M3_DYNAMIC: row_scales[i] = max(max_j |y_ij|, 1e-12) / 448,
+ *                              out[i, j] = e4m3(y_ij * (1 / row_scales[i]))
+ * e4m3 conversion rounds to nearest even and saturates to +-448 (NaN stays NaN).
+ * `input` is not written unless out == input.  `scale` (one float) and
+ * `row_scales` (rows floats) are device pointers.  fp8 output needs
+ * hidden % 4 == 0 with 8-byte aligned input/weight/residual rows and 4-byte
+ * aligned output rows, and rows of at most 16384 vectors (262144 elements at
+ * full alignment).  Output row stride is in output elements.
+ */
+HPRN_API int hprn_rms_norm_out(void* out, const void* input, const void* weight, void* residual,
+                               int64_t rows, int64_t hidden, int64_t out_row_stride,
+                               int64_t input_row_stride, int64_t residual_row_stride, double eps,
+                               int dtype, int out_form, const float* scale, float* row_scales,
+                               void* stream, unsigned flags);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 HPRN_API const char* hprn_last_error(void);

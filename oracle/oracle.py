@@ -49,6 +49,12 @@ def _load():
         lib.oracle_to_f32.argtypes = [ctypes.c_int, u16p, f32p, i64]
         lib.oracle_from_f32.argtypes = [ctypes.c_int, f32p, u16p, i64]
         lib.oracle_num_threads.restype = ctypes.c_int
+        vp = ctypes.c_void_p
+        lib.oracle_rms_norm_out.argtypes = [ctypes.c_int, vp, u16p, u16p, vp, i64, i64, i64, i64,
+                                            i64, ctypes.c_double, ctypes.c_int, ctypes.c_float, vp]
+        lib.oracle_rms_norm_out.restype = None
+        lib.oracle_f32_to_e4m3.argtypes = [vp, vp, i64]
+        lib.oracle_f32_to_e4m3.restype = None
         _lib = lib
     return _lib
 
@@ -80,6 +86,36 @@ def fused_add_rms_norm(dtype: int, x: np.ndarray, w: np.ndarray, r: np.ndarray, 
     lib.oracle_fused_add_rms_norm(dtype, _u16(xo), _u16(wc), _u16(ro), rows, hidden, hidden,
                                   hidden, float(eps), ss_mode)
     return xo, ro
+
+
+def rms_norm_out(dtype: int, x: np.ndarray, w: np.ndarray, eps: float, r: np.ndarray | None = None,
+                 fp8: str | None = None, scale: float = 1.0):
+    """The generalised row op (rms_norm_oracle.c: oracle_rms_norm_out).
+
+    fp8: None (16-bit output), "static" (e4m3 of y / scale) or "dynamic"
+    (per-row scales).  Returns (out, residual or None, row_scales or None);
+    inputs are not modified."""
+    lib = _load()
+    hidden = x.shape[-1]
+    xc = np.ascontiguousarray(x, dtype=np.uint16)
+    rows = xc.size // hidden
+    wc = np.ascontiguousarray(w, dtype=np.uint16)
+    rc = None if r is None else np.ascontiguousarray(r, dtype=np.uint16).copy()
+    out = np.empty(xc.shape, dtype=np.uint8 if fp8 else np.uint16)
+    scales = np.zeros(rows, dtype=np.float32) if fp8 == "dynamic" else None
+    lib.oracle_rms_norm_out(dtype, out.ctypes.data, _u16(xc), _u16(wc),
+                            None if rc is None else rc.ctypes.data, rows, hidden, hidden, hidden,
+                            hidden, float(eps), 1 if fp8 else 0, float(scale),
+                            None if scales is None else scales.ctypes.data)
+    return out, rc, scales
+
+
+def f32_to_e4m3(vals: np.ndarray) -> np.ndarray:
+    lib = _load()
+    v = np.ascontiguousarray(vals, dtype=np.float32)
+    out = np.empty(v.shape, dtype=np.uint8)
+    lib.oracle_f32_to_e4m3(v.ctypes.data, out.ctypes.data, v.size)
+    return out
 
 
 def relu(dtype: int, x: np.ndarray) -> np.ndarray:

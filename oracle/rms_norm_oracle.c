@@ -36,6 +36,7 @@
  */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #ifdef _OPENMP
@@ -132,6 +133,100 @@ void oracle_fused_add_rms_norm(int dtype, uint16_t* input, const uint16_t* weigh
   for (int64_t i = 0; i < rows; ++i) {
     fused_add_rms_norm_row(dtype, input + i * in_stride, weight, residual + i * res_stride,
                            hidden, eps, ss_mode);
+  }
+}
+
+/* ---- fp8 e4m3 (OCP "E4M3FN": bias 7, no infinities, max 448, NaN 0x7f) ---
+ * Round to nearest even, saturating to +-448 (the "satfinite" rule), NaN to
+ * 0x7f: written from the format definition. */
+static uint8_t f32_to_e4m3_satfinite(float f) {
+  if (f != f) return 0x7f;
+  uint8_t sign = signbit(f) ? 0x80 : 0x00;
+  float a = fabsf(f);
+  if (a >= 448.0f) return (uint8_t)(sign | 0x7e);
+  /* Smallest normal 2^-6; subnormals step by 2^-9. */
+  int e;
+  float m = frexpf(a, &e); /* a = m * 2^e, m in [0.5, 1) */
+  int exp_unbiased = e - 1;  /* a = 1.xxx * 2^(e-1) */
+  float quantum = exp_unbiased < -6 ? ldexpf(1.0f, -9) : ldexpf(1.0f, exp_unbiased - 3);
+  float q = a / quantum;            /* exact: power-of-two scaling */
+  float r = nearbyintf(q);          /* ties to even under the default rounding mode */
+  float v = r * quantum;
+  if (v >= 448.0f) return (uint8_t)(sign | 0x7e);
+  if (v == 0.0f) return sign;
+  int ve;
+  float vm = frexpf(v, &ve);
+  int ue = ve - 1;
+  if (ue < -6) { /* subnormal: mantissa = v / 2^-9 */
+    return (uint8_t)(sign | (uint8_t)(v / ldexpf(1.0f, -9)));
+  }
+  int mant = (int)((vm * 2.0f - 1.0f) * 8.0f); /* 3 fraction bits */
+  return (uint8_t)(sign | (uint8_t)((ue + 7) << 3) | (uint8_t)mant);
+}
+
+void oracle_f32_to_e4m3(const float* in, uint8_t* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = f32_to_e4m3_satfinite(in[i]);
+}
+
+/*
+ * The generalised row operation (an extension past the reference, which only
+ * has the in-place fused form): RMSNorm with or without the residual add, its
+ * output either 16-bit (T) or fp8 e4m3.
+ *   residual == NULL: s_j = f32(x_j)                           (plain RMSNorm)
+ *   otherwise:        s_j = f32(x_j) + f32(r_j), r_j <- round_T(s_j), and
+ *                     the normalised value uses the rounded residual.
+ *   y_j = (v_j * f32(w_j)) * inv, v_j = rounded residual or f32(x_j),
+ *   inv = rsqrt(eps + sum s_j^2 / H).
+ *   out_fp8 == 0: out_j = round_T(y_j)
+ *   static scale (row_scales == NULL): out_j = e4m3(y_j * (1 / scale))
+ *   dynamic (row_scales != NULL): amax = max_j |y_j| (NaNs ignored),
+ *     scale_i = max(amax, 1e-12) / 448, out_j = e4m3(y_j * (1 / scale_i)),
+ *     row_scales[i] = scale_i.
+ * The input is left unchanged unless out == input.
+ */
+void oracle_rms_norm_out(int dtype, void* out, const uint16_t* input, const uint16_t* weight,
+                         uint16_t* residual, int64_t rows, int64_t hidden, int64_t out_stride,
+                         int64_t in_stride, int64_t res_stride, double eps, int out_fp8,
+                         float scale, float* row_scales) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    const uint16_t* x = input + i * in_stride;
+    uint16_t* r = residual ? residual + i * res_stride : 0;
+    double ss = 0.0;
+    float* v = (float*)malloc(sizeof(float) * (size_t)hidden);
+    for (int64_t j = 0; j < hidden; ++j) {
+      float s = to_f32(dtype, x[j]);
+      if (r) {
+        s = s + to_f32(dtype, r[j]);
+        r[j] = from_f32(dtype, s);
+        v[j] = to_f32(dtype, r[j]);
+      } else {
+        v[j] = s;
+      }
+      ss += (double)s * (double)s;
+    }
+    float inv = (float)(1.0 / sqrt(ss / (double)hidden + eps));
+    float inv_scale = 1.0f;
+    if (out_fp8) {
+      if (row_scales) {
+        float amax = 0.0f;
+        for (int64_t j = 0; j < hidden; ++j) amax = fmaxf(amax, fabsf(v[j] * to_f32(dtype, weight[j]) * inv));
+        float sc = fmaxf(amax, 1e-12f) / 448.0f;
+        row_scales[i] = sc;
+        inv_scale = 1.0f / sc;
+      } else {
+        inv_scale = 1.0f / scale;
+      }
+    }
+    for (int64_t j = 0; j < hidden; ++j) {
+      float y = v[j] * to_f32(dtype, weight[j]) * inv;
+      if (out_fp8) {
+        ((uint8_t*)out)[i * out_stride + j] = f32_to_e4m3_satfinite(y * inv_scale);
+      } else {
+        ((uint16_t*)out)[i * out_stride + j] = from_f32(dtype, y);
+      }
+    }
+    free(v);
   }
 }
 

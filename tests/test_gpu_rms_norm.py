@@ -305,3 +305,24 @@ def test_launch_flags_validated(cuda):
     x, w, r, eps = make_inputs(4, 256, torch.bfloat16, "c0", seed=1, device=cuda)
     with pytest.raises(capi.HprnError, match="unknown launch flags"):
         capi.rms_norm_tensors(x, w, r, eps, flags=0x80)
+
+
+def test_torch_compile_fullgraph(cuda):
+    """The mutation-annotated schemas and Meta kernels let torch.compile trace
+    the ops with fullgraph=True; results match eager bit for bit."""
+    import hp_rms_norm_b200
+
+    def block(x, r, w, out):
+        hp_rms_norm_b200.hp_rms_norm(x, w, r, 1e-6)
+        hp_rms_norm_b200.relu(out, x)
+        return out * 2
+
+    x0, w, r0, _ = make_inputs(64, 4096, torch.bfloat16, "c0", seed=17, device=cuda)
+    xe, re, oe = x0.clone(), r0.clone(), torch.empty_like(x0)
+    want = block(xe, re, w, oe)
+    compiled = torch.compile(block, fullgraph=True)
+    xc, rc, oc = x0.clone(), r0.clone(), torch.empty_like(x0)
+    got = compiled(xc, rc, w, oc)
+    torch.cuda.synchronize()
+    for a, b in ((want, got), (xe, xc), (re, rc), (oe, oc)):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
