@@ -67,7 +67,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["sweep", "config0", "shard", "decode", "relu"],
+    ap.add_argument("--workload",
+                    choices=["sweep", "config0", "shard", "decode", "relu", "variants", "act"],
                     default="sweep")
     ap.add_argument("--hidden", default=None,
                     help="comma-separated hidden sizes: restrict the sweep (e.g. for ncu captures)")
@@ -345,6 +346,10 @@ def run_ours(args, dist):
     elif args.workload == "decode":
         shapes = [(r, h) for r in DECODE_ROWS for h in DECODE_HIDDEN]
         workload = "config2 shapes (bf16): rows {1,7,33,128,512} x hidden {4096,5120,7168,8192}"
+    elif args.workload == "variants":
+        return run_variants(args, dist, dev, stream)
+    elif args.workload == "act":
+        return run_act(args, dist, dev, stream)
     else:
         return run_relu(args, dist, dev, stream)
 
@@ -502,17 +507,22 @@ def run_e2e(args, shapes, bufs, stream, dev, dist, eps):
                      torch.empty_like(x, device="cpu").pin_memory(),
                      torch.empty_like(r, device="cpu").pin_memory()))
     streams = [torch.cuda.Stream(device=dev) for _ in range(3)]
-    chunk_bytes = 32 << 20
+    chunk_bytes = 64 << 20  # input + residual bytes per chunk
     h2d = sum(x.numel() * 2 + r.numel() * 2 + w.numel() * 2 for x, w, r in bufs)
     d2h = sum(x.numel() * 2 + r.numel() * 2 for x, w, r in bufs)
 
     def step():
+        main = torch.cuda.current_stream()
+        for (_, w, _), (_, hw, _, _, _) in zip(bufs, host):
+            w.copy_(hw, non_blocking=True)
+        for s in streams:
+            s.wait_stream(main)
+        # Every shape's row chunks rotate over the streams without a join in
+        # between, so host->device copies of one chunk overlap device->host
+        # copies of another across shape boundaries too.
         c = 0
         for (rows, h), (x, w, r), (hx, hw, hr, ox, orr) in zip(shapes, bufs, host):
             per = max(1, chunk_bytes // (h * 2 * 2))
-            w.copy_(hw, non_blocking=True)
-            for s in streams:
-                s.wait_stream(torch.cuda.current_stream())
             for r0 in range(0, rows, per):
                 r1 = min(rows, r0 + per)
                 s = streams[c % len(streams)]
@@ -524,8 +534,8 @@ def run_e2e(args, shapes, bufs, stream, dev, dist, eps):
                                   h, h, h, eps, capi.DTYPE_BF16, s.cuda_stream)
                     ox[r0:r1].copy_(x[r0:r1], non_blocking=True)
                     orr[r0:r1].copy_(r[r0:r1], non_blocking=True)
-            for s in streams:
-                torch.cuda.current_stream().wait_stream(s)
+        for s in streams:
+            main.wait_stream(s)
 
     for _ in range(1):
         step()
@@ -544,6 +554,139 @@ def run_e2e(args, shapes, bufs, stream, dev, dist, eps):
     return {"value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
             "steps": K, "api": "hprn_rms_norm (C ABI) on pinned-host-staged buffers, 3 streams"}
+
+
+VARIANT_HIDDEN = [2048, 4096, 8192, 16384, 32768]
+# name -> (residual?, output form, algorithmic bytes per element)
+VARIANTS = {
+    "fused_in_place": (True, "same", 8),
+    "fused_out_of_place": (True, "same", 8),
+    "plain": (False, "same", 4),
+    "fused_fp8_static": (True, "fp8s", 7),
+    "fused_fp8_dynamic": (True, "fp8d", 7),
+    "plain_fp8_dynamic": (False, "fp8d", 3),
+}
+
+
+def run_variants(args, dist, dev, stream):
+    """Extended forms (plain RMSNorm, out-of-place, fp8 outputs) at batch 4096
+    bf16 and hidden 2048..32768: per-variant GB/s over its algorithmic bytes
+    (inputs read once, outputs written once; fp8 output 1 byte per element,
+    plus 4 bytes per row of scales for the dynamic form), each shape timed as
+    graph replays over rotating cold buffers."""
+    import torch
+
+    from hp_rms_norm_b200 import capi
+
+    rows = args.rows
+    peak, peak_src = measured_peak()
+    results = {}
+    for name, (res, form, bpe) in VARIANTS.items():
+        per = []
+        for h in ([int(x) for x in args.hidden.split(",")] if args.hidden else VARIANT_HIDDEN):
+            set_bytes = rows * h * 2 * 2
+            nsets = max(2, int(-(-600e6 // set_bytes)))
+            xs = [torch.randn(rows, h, device=dev).to(torch.bfloat16) for _ in range(nsets)]
+            rs = [torch.randn(rows, h, device=dev).to(torch.bfloat16) for _ in range(nsets)]
+            w = (1 + 0.1 * torch.randn(h, device=dev)).to(torch.bfloat16)
+            if form == "same":
+                outs = xs if name == "fused_in_place" else \
+                    [torch.empty(rows, h, device=dev, dtype=torch.bfloat16) for _ in range(nsets)]
+            else:
+                outs = [torch.empty(rows, h, device=dev, dtype=torch.float8_e4m3fn)
+                        for _ in range(nsets)]
+            scale = torch.tensor([0.01], device=dev)
+            rsc = torch.empty(rows, device=dev)
+            ocode = {"same": capi.OUT_SAME, "fp8s": capi.OUT_FP8_E4M3_STATIC,
+                     "fp8d": capi.OUT_FP8_E4M3_DYNAMIC}[form]
+
+            def call(k, sh, h=h, xs=xs, rs=rs, w=w, outs=outs, ocode=ocode, res=res):
+                capi.rms_norm_out(outs[k].data_ptr(), xs[k].data_ptr(), w.data_ptr(),
+                                  rs[k].data_ptr() if res else None, rows, h, h, h, h, 1e-6,
+                                  capi.DTYPE_BF16, ocode, scale.data_ptr(), rsc.data_ptr(), sh)
+
+            L = max(16, nsets)
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                call(0, s.cuda_stream)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for k in range(L):
+                    call(k % nsets, s.cuda_stream)
+            g.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(3):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (3 * L)
+            byt = rows * h * bpe + h * 2 + (rows * 4 if form == "fp8d" else 0)
+            per.append({"hidden": h, "us": round(us, 2), "gbs": round(byt / us / 1e3, 1),
+                        "frac": round(byt / us / 1e3 / peak, 3)})
+            del g, xs, rs, outs
+            torch.cuda.empty_cache()
+        tot_b = sum(e["gbs"] * e["us"] for e in per)
+        tot_t = sum(e["us"] for e in per)
+        results[name] = {"gbs": round(tot_b / tot_t, 1), "frac": round(tot_b / tot_t / peak, 3),
+                         "per_shape": per}
+    value = statistics.mean(v["gbs"] for v in results.values())
+    return {"metric": "extended RMSNorm forms: achieved HBM GB/s (bf16 input, batch 4096)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": dist.world, "steps": 3,
+            "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic N(0,1)",
+            "config": {"workload": "variants", "rows": rows,
+                       "hidden": [e["hidden"] for e in next(iter(results.values()))["per_shape"]],
+                       "bytes_per_element": {k: v[2] for k, v in VARIANTS.items()},
+                       "l2": "cold: rotating buffer sets >= 600 MB, graph replays"},
+            "peak": peak, "peak_source": peak_src, "variants": results}
+
+
+def run_act(args, dist, dev, stream):
+    """Gated activations (silu/gelu/gelu_tanh-and-mul) on a [4096, 2 x 14336]
+    bf16 input (an LLM MLP's gate/up projection): GB/s over 6 bytes per output
+    element (gate and up read, out written)."""
+    import torch
+
+    from hp_rms_norm_b200 import capi
+
+    rows, d = args.rows, 14336
+    peak, peak_src = measured_peak()
+    nsets = 3
+    xs = [torch.randn(rows, 2 * d, device=dev).to(torch.bfloat16) for _ in range(nsets)]
+    outs = [torch.empty(rows, d, device=dev, dtype=torch.bfloat16) for _ in range(nsets)]
+    results = {}
+    for name, act in (("silu", capi.ACT_SILU), ("gelu", capi.ACT_GELU),
+                      ("gelu_tanh", capi.ACT_GELU_TANH)):
+        def step(k, sh, act=act):
+            capi.act_and_mul(outs[k].data_ptr(), xs[k].data_ptr(), rows, d, d, 2 * d, act,
+                             capi.DTYPE_BF16, sh)
+
+        with torch.cuda.stream(stream):
+            for k in range(args.warmup):
+                step(k % nsets, stream.cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(args.steps):
+            step(k % nsets, stream.cuda_stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        byt = rows * d * 6
+        results[name] = {"us": round(us, 2), "gbs": round(byt / us / 1e3, 1),
+                         "frac": round(byt / us / 1e3 / peak, 3)}
+    value = statistics.mean(v["gbs"] for v in results.values())
+    return {"metric": "gated activation (act(gate) * up) achieved HBM GB/s", "value": round(value, 1),
+            "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1)",
+            "config": {"workload": f"act_and_mul [{rows}, 2x{d}] bf16",
+                       "l2": "3 rotating input/output sets of 352 MB"},
+            "peak": peak, "peak_source": peak_src, "activations": results}
 
 
 def run_relu(args, dist, dev, stream):

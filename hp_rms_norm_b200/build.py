@@ -27,7 +27,7 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(ROOT, "_build")
 LIB_NAME = "libhp_rms_norm_b200.so"
 LIB = os.path.join(PKG, LIB_NAME)
-CUDA_SOURCES = ["rms_norm.cu", "relu.cu", "runtime.cu"]
+CUDA_SOURCES = ["rms_norm.cu", "relu.cu", "act_and_mul.cu", "runtime.cu"]
 HEADERS = ["vec.cuh", "runtime.cuh"]
 
 NVCC_FLAGS = [

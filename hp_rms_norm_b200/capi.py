@@ -25,6 +25,10 @@ ERR_CUDA = -4
 LAUNCH_PDL = 1
 LAUNCH_DEFAULT = LAUNCH_PDL
 
+ACT_SILU = 0
+ACT_GELU = 1
+ACT_GELU_TANH = 2
+
 OUT_SAME = 0
 OUT_FP8_E4M3_STATIC = 1
 OUT_FP8_E4M3_DYNAMIC = 2
@@ -36,6 +40,7 @@ EXPORTED = (
     "hprn_rms_norm_ex",
     "hprn_relu_ex",
     "hprn_rms_norm_out",
+    "hprn_act_and_mul",
     "hprn_last_error",
     "hprn_status_string",
     "hprn_version",
@@ -76,6 +81,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_rms_norm_out.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, ctypes.c_double,
                                       c_int, c_int, vp, vp, vp, u32]
     lib.hprn_rms_norm_out.restype = c_int
+    lib.hprn_act_and_mul.argtypes = [vp, vp, i64, i64, i64, i64, c_int, c_int, vp, u32]
+    lib.hprn_act_and_mul.restype = c_int
     lib.hprn_last_error.argtypes = []
     lib.hprn_last_error.restype = ctypes.c_char_p
     lib.hprn_status_string.argtypes = [c_int]
@@ -131,6 +138,13 @@ def rms_norm_out(out_ptr: int, input_ptr: int, weight_ptr: int, residual_ptr: in
     _check(load().hprn_rms_norm_out(out_ptr, input_ptr, weight_ptr, residual_ptr, rows, hidden,
                                     out_row_stride, input_row_stride, residual_row_stride, eps,
                                     dtype, out_form, scale_ptr, row_scales_ptr, stream, flags))
+
+
+def act_and_mul(out_ptr: int, input_ptr: int, rows: int, d: int, out_row_stride: int,
+                input_row_stride: int, act: int, dtype: int, stream: int = 0,
+                flags: int = LAUNCH_DEFAULT) -> None:
+    _check(load().hprn_act_and_mul(out_ptr, input_ptr, rows, d, out_row_stride, input_row_stride,
+                                   act, dtype, stream, flags))
 
 
 def plan(rows: int, hidden: int, dtype: int = DTYPE_BF16, input_ptr: int = 0,
@@ -204,3 +218,15 @@ def rms_norm_out_tensors(out, inp, weight, res, eps: float, scale=None, row_scal
                  inp.stride(0), res.stride(0) if res is not None else hidden, eps, dtype_code(inp),
                  form, scale.data_ptr() if scale is not None else None,
                  row_scales.data_ptr() if row_scales is not None else None, stream, flags)
+
+
+def act_and_mul_tensors(out, inp, act: int, stream: int | None = None,
+                        flags: int = LAUNCH_DEFAULT) -> None:
+    """hprn_act_and_mul on 2-D CUDA tensors: inp [rows, 2d] -> out [rows, d]."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(inp.device).cuda_stream
+    rows, d = out.shape
+    act_and_mul(out.data_ptr(), inp.data_ptr(), rows, d, out.stride(0), inp.stride(0), act,
+                dtype_code(inp), stream, flags)

@@ -211,6 +211,36 @@ void rms_norm_fp8(at::Tensor& out, const at::Tensor& input, const at::Tensor& we
                                  rsp, stream, HPRN_LAUNCH_DEFAULT));
 }
 
+// out[..., d] = act(input[..., :d]) * input[..., d:]  (extension past the reference).
+void act_and_mul(at::Tensor& out, const at::Tensor& input, int act) {
+  TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 2 == 0, "input.size(-1) must be even");
+  const int64_t d = input.size(-1) / 2;
+  TORCH_CHECK(out.dim() == input.dim(), "out.dim() == input.dim()");
+  for (int64_t i = 0; i + 1 < input.dim(); ++i)
+    TORCH_CHECK(out.size(i) == input.size(i), "out and input must agree on leading dimensions");
+  TORCH_CHECK(out.size(-1) == d, "out.size(-1) == input.size(-1) / 2");
+  TORCH_CHECK(input.is_cuda() && out.is_cuda() && out.device() == input.device(),
+              "out and input must be CUDA tensors on the same device");
+  TORCH_CHECK(out.scalar_type() == input.scalar_type(), "out and input must have the same dtype");
+  const int dtype = dtype_code(input);
+  if (out.numel() == 0) return;
+  TORCH_CHECK(input.stride(-1) == 1 && (d == 1 || out.stride(-1) == 1),
+              "input and out must be contiguous in the last dimension");
+  int64_t rows = 0, is = 0, orows = 0, os = 0;
+  rows_of(input, "input", &rows, &is);
+  rows_of(out, "out", &orows, &os);
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_act_and_mul(out.data_ptr(), input.data_ptr(), rows, d, os, is, act, dtype,
+                                stream, HPRN_LAUNCH_DEFAULT));
+}
+
+void silu_and_mul(at::Tensor& out, const at::Tensor& input) { act_and_mul(out, input, HPRN_ACT_SILU); }
+void gelu_and_mul(at::Tensor& out, const at::Tensor& input) { act_and_mul(out, input, HPRN_ACT_GELU); }
+void gelu_tanh_and_mul(at::Tensor& out, const at::Tensor& input) {
+  act_and_mul(out, input, HPRN_ACT_GELU_TANH);
+}
+
 // Shape-only kernels for tracing (torch.compile / FakeTensor): the ops return
 // nothing and only mutate their annotated arguments.
 void rms_norm_meta(at::Tensor&, const at::Tensor&, at::Tensor&, double) {}
@@ -220,6 +250,7 @@ void rms_norm_out_meta(at::Tensor&, const at::Tensor&, const at::Tensor&,
 void rms_norm_fp8_meta(at::Tensor&, const at::Tensor&, const at::Tensor&,
                        c10::optional<at::Tensor>, double, c10::optional<at::Tensor>,
                        c10::optional<at::Tensor>) {}
+void act_and_mul_meta(at::Tensor&, const at::Tensor&) {}
 
 }  // namespace
 
@@ -232,6 +263,10 @@ TORCH_LIBRARY(hp_rms_norm, m) {
         "float eps) -> ()");
   m.def("rms_norm_fp8(Tensor(a!) out, Tensor input, Tensor weight, Tensor(b!)? residual, "
         "float eps, Tensor? scale, Tensor(c!)? row_scales) -> ()");
+  // Extensions: gated activations.
+  m.def("silu_and_mul(Tensor(a!) out, Tensor input) -> ()");
+  m.def("gelu_and_mul(Tensor(a!) out, Tensor input) -> ()");
+  m.def("gelu_tanh_and_mul(Tensor(a!) out, Tensor input) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(hp_rms_norm, CUDA, m) {
@@ -239,6 +274,9 @@ TORCH_LIBRARY_IMPL(hp_rms_norm, CUDA, m) {
   m.impl("relu", &relu);
   m.impl("rms_norm_out", &rms_norm_out);
   m.impl("rms_norm_fp8", &rms_norm_fp8);
+  m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("gelu_and_mul", &gelu_and_mul);
+  m.impl("gelu_tanh_and_mul", &gelu_tanh_and_mul);
 }
 
 TORCH_LIBRARY_IMPL(hp_rms_norm, Meta, m) {
@@ -246,4 +284,7 @@ TORCH_LIBRARY_IMPL(hp_rms_norm, Meta, m) {
   m.impl("relu", &relu_meta);
   m.impl("rms_norm_out", &rms_norm_out_meta);
   m.impl("rms_norm_fp8", &rms_norm_fp8_meta);
+  m.impl("silu_and_mul", &act_and_mul_meta);
+  m.impl("gelu_and_mul", &act_and_mul_meta);
+  m.impl("gelu_tanh_and_mul", &act_and_mul_meta);
 }

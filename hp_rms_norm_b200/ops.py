@@ -9,7 +9,8 @@ and returns None; ``relu(output, input)`` writes ``torch.relu(input)`` into
 Extensions (not in the reference): ``rms_norm`` (plain RMSNorm),
 ``fused_add_rms_norm`` (the fused op into a separate output) and
 ``rms_norm_fp8`` (either form with an fp8 e4m3 output, static or per-row
-scale).  Everything dispatches through ``torch.ops.hp_rms_norm``, registered
+scale), and the gated activations ``silu_and_mul``, ``gelu_and_mul`` and
+``gelu_tanh_and_mul``.  Everything dispatches through ``torch.ops.hp_rms_norm``, registered
 by this package's compiled ``_C`` extension.
 """
 import torch
@@ -65,4 +66,28 @@ def rms_norm_fp8(input, weight, eps, residual=None, scale=None, out=None):
     return out, row_scales
 
 
-__all__ = ["hp_rms_norm", "relu", "rms_norm", "fused_add_rms_norm", "rms_norm_fp8", "torch"]
+def _act_and_mul(op, input, out):
+    if out is None:
+        out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), dtype=input.dtype,
+                          device=input.device)
+    op(out, input)
+    return out
+
+
+def silu_and_mul(input, out=None):
+    """out = silu(input[..., :d]) * input[..., d:], d = input.shape[-1] // 2."""
+    return _act_and_mul(torch.ops.hp_rms_norm.silu_and_mul.default, input, out)
+
+
+def gelu_and_mul(input, out=None):
+    """out = gelu(input[..., :d]) * input[..., d:] (erf form)."""
+    return _act_and_mul(torch.ops.hp_rms_norm.gelu_and_mul.default, input, out)
+
+
+def gelu_tanh_and_mul(input, out=None):
+    """out = gelu_tanh(input[..., :d]) * input[..., d:] (tanh approximation)."""
+    return _act_and_mul(torch.ops.hp_rms_norm.gelu_tanh_and_mul.default, input, out)
+
+
+__all__ = ["hp_rms_norm", "relu", "rms_norm", "fused_add_rms_norm", "rms_norm_fp8",
+           "silu_and_mul", "gelu_and_mul", "gelu_tanh_and_mul", "torch"]

@@ -2,6 +2,8 @@
 
     python -m hp_rms_norm_b200.tune [--rows 4096] [--hidden 1024,2048,...]
                                     [--dtype bf16|fp16] [--warm] [--json out.json]
+                                    [--variant fused|fused_out|plain|fused_fp8s|fused_fp8d|
+                                               plain_fp8s|plain_fp8d]
 
 Times every compiled launch plan that covers each requested shape (through
 ``hprn_set_plan_override``) and prints the fastest, next to the built-in
@@ -21,15 +23,31 @@ import math
 SWEEP = [1024 * i for i in range(1, 17)] + [20480, 24576, 28672, 32768]
 
 
-def candidates(nvec: int) -> list[str]:
-    """Plans (32-byte vectors) whose threads x vectors x CTAs cover nvec vectors."""
+# variant: (adds a residual, output form, algorithmic bytes per element)
+VARIANTS = {
+    "fused": (True, "same", 8),        # the reference's in-place form
+    "fused_out": (True, "same", 8),
+    "plain": (False, "same", 4),
+    "fused_fp8s": (True, "fp8s", 7),
+    "fused_fp8d": (True, "fp8d", 7),
+    "plain_fp8s": (False, "fp8s", 3),
+    "plain_fp8d": (False, "fp8d", 3),
+}
+
+
+def candidates(nvec: int, full: bool = True) -> list[str]:
+    """Plans (32-byte vectors) whose threads x vectors x CTAs cover nvec vectors
+    (full: the in-place fused form's plan set; else the extended forms' set)."""
     out = []
+    warp_vpts = (1, 2, 3, 4) if full else (1, 2, 4)
+    cta_vpts = (1, 2, 3, 4, 6, 8) if full else (1, 2, 4)
     if nvec <= 128:
-        for vpt in (1, 2, 3, 4):
-            if vpt * 32 >= nvec > (vpt - 1) * 32:
-                out += [f"warp:vec32:vpt{vpt}:tpr32:cluster1:rpc{r}" for r in (2, 4, 8)]
+        vpt = min(v for v in warp_vpts if v * 32 >= nvec)
+        out += [f"warp:vec32:vpt{vpt}:tpr32:cluster1:rpc{r}" for r in (2, 4, 8)]
     for cl in (1, 2, 4, 8):
-        for vpt in (1, 2, 3, 4, 6, 8):
+        for vpt in cta_vpts:
+            if cl > 1 and not full and vpt == 1:
+                continue
             max_threads = 1024 if vpt <= 2 else (512 if vpt <= 4 else 256)
             sl = -(-nvec // cl)
             tpr = -(-(-(-sl // vpt)) // 32) * 32
@@ -37,6 +55,12 @@ def candidates(nvec: int) -> list[str]:
                 continue
             kind = "cta" if cl == 1 else "cluster"
             out.append(f"{kind}:vec32:vpt{vpt}:tpr{tpr}:cluster{cl}:rpc1")
+    # Persistent CTAs with the next row prefetched (one CTA covers the row).
+    for vpt in (1, 2, 4):
+        tpr = -(-(-(-nvec // vpt)) // 32) * 32
+        if 32 <= tpr <= (1024 if vpt == 1 else 512 if vpt == 2 else 256) and \
+                not (tpr > 32 and (tpr - 32) * vpt >= nvec):
+            out.append(f"persist:vec32:vpt{vpt}:tpr{tpr}:cluster1:rpc1")
     return out
 
 
@@ -62,10 +86,15 @@ def graph_us(torch, fn, nsets: int, reps: int = 3) -> float:
     return e0.elapsed_time(e1) * 1e3 / (reps * L)
 
 
-def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False) -> dict:
+def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False,
+          variant: str = "fused") -> dict:
     import torch
 
     from . import capi
+
+    res_needed, form_name, bpe = VARIANTS[variant]
+    form = {"same": capi.OUT_SAME, "fp8s": capi.OUT_FP8_E4M3_STATIC,
+            "fp8d": capi.OUT_FP8_E4M3_DYNAMIC}[form_name]
 
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     code = capi.DTYPE_BF16 if dtype == "bf16" else capi.DTYPE_FP16
@@ -77,27 +106,40 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
         xs = [torch.randn(rows, h, device=dev).to(tdt) for _ in range(nsets)]
         rs = [torch.randn(rows, h, device=dev).to(tdt) for _ in range(nsets)]
         w = (1 + 0.1 * torch.randn(h, device=dev)).to(tdt)
-        byt = 4 * rows * h * 2 + 2 * h
+        fp8 = form != capi.OUT_SAME
+        if variant == "fused":
+            outs = xs
+        else:
+            outs = [torch.empty(rows, h, device=dev,
+                                dtype=torch.float8_e4m3fn if fp8 else tdt) for _ in range(nsets)]
+        scale = torch.tensor([0.01], device=dev)
+        row_scales = torch.empty(rows, device=dev)
+        byt = rows * h * bpe + 2 * h + (4 * rows if form_name == "fp8d" else 0)
 
         def run(k, s):
-            capi.rms_norm(xs[k].data_ptr(), w.data_ptr(), rs[k].data_ptr(), rows, h, h, h, 1e-6,
-                          code, s)
+            capi.rms_norm_out(outs[k].data_ptr(), xs[k].data_ptr(), w.data_ptr(),
+                              rs[k].data_ptr() if res_needed else None, rows, h, h, h, h, 1e-6,
+                              code, form, scale.data_ptr(), row_scales.data_ptr(), s)
 
         timings = {}
         try:
-            for p in candidates(h // 16) if h % 16 == 0 else []:
+            for p in candidates(h // 16, variant == "fused") if h % 16 == 0 else []:
                 capi.set_plan_override(p)
-                timings[p] = round(graph_us(torch, run, nsets), 2)
+                try:
+                    timings[p] = round(graph_us(torch, run, nsets), 2)
+                except capi.HprnError:
+                    pass  # plan not compiled for this variant (e.g. over its launch bound)
         finally:
             capi.set_plan_override(None)
-        default = capi.plan(rows, h, code, xs[0].data_ptr(), rs[0].data_ptr())
+        default = capi.plan(rows, h, code, xs[0].data_ptr(), rs[0].data_ptr()) \
+            if variant == "fused" else "default"
         t_default = round(graph_us(torch, run, nsets), 2)
         best = min(timings, key=timings.get) if timings else default
         results[h] = {"default": default, "default_us": t_default,
                       "default_gbs": round(byt / t_default / 1e3, 1),
                       "best": best, "best_us": timings.get(best, t_default),
-                      "plans": timings, "buffer_sets": nsets}
-        del xs, rs
+                      "plans": timings, "buffer_sets": nsets, "bytes_per_launch": byt}
+        del xs, rs, outs
         torch.cuda.empty_cache()
     return results
 
@@ -109,8 +151,9 @@ def main() -> None:
     ap.add_argument("--dtype", choices=["bf16", "fp16"], default="bf16")
     ap.add_argument("--warm", action="store_true")
     ap.add_argument("--json", default=None)
+    ap.add_argument("--variant", choices=list(VARIANTS), default="fused")
     a = ap.parse_args()
-    res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm)
+    res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm, a.variant)
     print(f"{'hidden':>7} {'default plan':40} {'us':>8} {'GB/s':>8}   {'best plan':40} {'us':>8}")
     for h, r in res.items():
         print(f"{h:>7} {r['default']:40} {r['default_us']:>8} {r['default_gbs']:>8}   "

@@ -59,6 +59,13 @@ typedef enum hprn_out_form {
   HPRN_OUT_FP8_E4M3_DYNAMIC = 2   /* fp8 e4m3, one scale per row, written to row_scales */
 } hprn_out_form;
 
+/* Activations of hprn_act_and_mul. */
+typedef enum hprn_act {
+  HPRN_ACT_SILU = 0,      /* a / (1 + exp(-a))                                   */
+  HPRN_ACT_GELU = 1,      /* a / 2 * (1 + erf(a / sqrt(2)))                      */
+  HPRN_ACT_GELU_TANH = 2  /* a / 2 * (1 + tanh(sqrt(2/pi) * (a + 0.044715 a^3))) */
+} hprn_act;
+
 typedef enum hprn_status {
   HPRN_OK = 0,
   HPRN_ERR_INVALID_ARGUMENT = -1, /* bad size, stride, null pointer, overlap */
@@ -145,6 +152,17 @@ HPRN_API int hprn_rms_norm_out(void* out, const void* input, const void* weight,
                                int64_t input_row_stride, int64_t residual_row_stride, double eps,
                                int dtype, int out_form, const float* scale, float* row_scales,
                                void* stream, unsigned flags);
+
+/*
+ * Gated activation (an extension past the reference):
+ *   out[i, j] = round_T(act(f32(input[i, j])) * f32(input[i, d + j])),  j < d
+ * Input rows hold [gate | up] (2d elements), output rows d elements; fp32
+ * arithmetic with CUDA's expf / erff / tanhf.  out and input must not overlap.
+ * Strides are in elements.  `act` is an hprn_act value.
+ */
+HPRN_API int hprn_act_and_mul(void* out, const void* input, int64_t rows, int64_t d,
+                              int64_t out_row_stride, int64_t input_row_stride, int act,
+                              int dtype, void* stream, unsigned flags);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 HPRN_API const char* hprn_last_error(void);

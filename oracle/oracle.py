@@ -55,6 +55,8 @@ def _load():
         lib.oracle_rms_norm_out.restype = None
         lib.oracle_f32_to_e4m3.argtypes = [vp, vp, i64]
         lib.oracle_f32_to_e4m3.restype = None
+        lib.oracle_act_and_mul.argtypes = [ctypes.c_int, ctypes.c_int, u16p, u16p, i64, i64]
+        lib.oracle_act_and_mul.restype = None
         _lib = lib
     return _lib
 
@@ -115,6 +117,19 @@ def f32_to_e4m3(vals: np.ndarray) -> np.ndarray:
     v = np.ascontiguousarray(vals, dtype=np.float32)
     out = np.empty(v.shape, dtype=np.uint8)
     lib.oracle_f32_to_e4m3(v.ctypes.data, out.ctypes.data, v.size)
+    return out
+
+
+ACTS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}
+
+
+def act_and_mul(dtype: int, act: str, x: np.ndarray) -> np.ndarray:
+    """Gated activation on [rows, 2d] bit patterns -> [rows, d]."""
+    lib = _load()
+    xc = np.ascontiguousarray(x, dtype=np.uint16)
+    rows, two_d = xc.shape
+    out = np.empty((rows, two_d // 2), dtype=np.uint16)
+    lib.oracle_act_and_mul(dtype, ACTS[act], _u16(out), _u16(xc), rows, two_d // 2)
     return out
 
 

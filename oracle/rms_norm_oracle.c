@@ -243,6 +243,27 @@ void oracle_relu(int dtype, uint16_t* out, const uint16_t* in, int64_t n) {
   }
 }
 
+/* Gated activations: out[i, j] = round_T(act(x[i, j]) * x[i, d + j]) in fp32,
+ * act per the published GELU / SiLU definitions (0: silu, 1: gelu erf,
+ * 2: gelu tanh), with the C library's expf / erff / tanhf. */
+static float oracle_act(int act, float a) {
+  if (act == 0) return a / (1.0f + expf(-a));
+  if (act == 1) return 0.5f * a * (1.0f + erff(a * 0.70710678118654752f));
+  return 0.5f * a * (1.0f + tanhf(0.79788456080286536f * (a + 0.044715f * a * a * a)));
+}
+
+void oracle_act_and_mul(int dtype, int act, uint16_t* out, const uint16_t* in, int64_t rows,
+                        int64_t d) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    for (int64_t j = 0; j < d; ++j) {
+      float g = to_f32(dtype, in[i * 2 * d + j]);
+      float u = to_f32(dtype, in[i * 2 * d + d + j]);
+      out[i * d + j] = from_f32(dtype, oracle_act(act, g) * u);
+    }
+  }
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();
