@@ -41,10 +41,7 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include <map>
-#include <mutex>
 #include <string>
-#include <tuple>
 
 #include "runtime.cuh"
 #include "vec.cuh"
@@ -414,115 +411,6 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
 }
 
 // ---------------------------------------------------------------------------
-// Kernel 4 (listed before kernel 3 in this file): persistent CTAs, each
-// walking rows blockIdx.x, blockIdx.x + gridDim.x, ...  The next row's loads
-// are issued before the current row is reduced and written (two register sets
-// alternate), so a CTA keeps memory busy across its rows' reduce and store
-// phases; the weight slice is loaded once and held in registers for every row.
-// Largest CTA it is compiled for, by the registers two row sets plus the
-// weight take.
-__host__ __device__ constexpr int persist_max_threads(int vpt, bool res) {
-  return vpt <= 1 ? (res ? 512 : 1024) : (vpt <= 2 ? 512 : 256);
-}
-
-template <typename T, int VEC, int VPT, bool RES>
-__device__ __forceinline__ void persist_load(const RmsArgs& a, int64_t row, Vec<VEC> (&xv)[VPT],
-                                             Vec<VEC> (&rv)[VPT], uint64_t pol) {
-  constexpr int EPV = Vec<VEC>::kElems;
-  const uint16_t* xr = a.x + row * a.x_stride;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int v = threadIdx.x + j * blockDim.x;
-    if (v < a.nvec) {
-      xv[j] = ld_stream<VEC>(xr + static_cast<int64_t>(v) * EPV, pol);
-      if constexpr (RES) rv[j] = ld_stream<VEC>(a.r + row * a.r_stride + static_cast<int64_t>(v) * EPV, pol);
-    }
-  }
-}
-
-template <typename T, int VEC, int VPT, bool RES, int OUT>
-__device__ __forceinline__ void persist_row(const RmsArgs& a, int64_t row, Vec<VEC> (&xv)[VPT],
-                                            const Vec<VEC> (&rv)[VPT], const Vec<VEC> (&wv)[VPT],
-                                            float (&part)[32], float (&amax_part)[32],
-                                            float static_inv) {
-  constexpr int EPV = Vec<VEC>::kElems;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  const int nwarps = blockDim.x >> 5;
-  float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int v = tid + j * blockDim.x;
-    if (v < a.nvec) {
-      if constexpr (RES) {
-        add_round<T, VEC>(xv[j], rv[j], a0, a1);
-        st_global<VEC>(a.r + row * a.r_stride + static_cast<int64_t>(v) * EPV, xv[j]);
-      } else {
-        square_sum<T, VEC>(xv[j], a0, a1);
-      }
-    }
-  }
-  const float wsum = warp_sum(a0 + a1);
-  if (lane == 0) part[warp] = wsum;
-  __syncthreads();
-  const float total = warp_sum(lane < nwarps ? part[lane] : 0.f);
-  const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
-  float inv_scale = static_inv;
-  if constexpr (OUT == kOutFp8Dynamic) {
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j)
-      if (tid + j * static_cast<int>(blockDim.x) < a.nvec) m = vec_amax<T, VEC>(xv[j], wv[j], inv, m);
-    m = warp_max(m);
-    if (lane == 0) amax_part[warp] = m;
-    __syncthreads();
-    const float scale = fmaxf(warp_max(lane < nwarps ? amax_part[lane] : 0.f), kMinAmax) / kE4m3Max;
-    inv_scale = 1.0f / scale;
-    if (tid == 0) a.row_scales[row] = scale;
-  }
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int v = tid + j * blockDim.x;
-    if (v < a.nvec) store_out<T, VEC, OUT>(a, row, v, xv[j], wv[j], inv, inv_scale);
-  }
-}
-
-template <typename T, int VEC, int VPT, bool RES, int OUT>
-__global__ void __launch_bounds__(persist_max_threads(VPT, RES)) rms_norm_persist_rows(RmsArgs a) {
-  constexpr int EPV = Vec<VEC>::kElems;
-  // Partial-sum buffers alternate between consecutive rows: a fast warp can
-  // write row k+1's partial while slower warps still read row k's.
-  __shared__ float part[2][32];
-  __shared__ float amax_part[2][32];
-  pdl_entry();
-  const uint64_t pol_stream = policy_evict_first();
-  const uint64_t pol_keep = policy_evict_last();
-  Vec<VEC> wv[VPT];
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int v = threadIdx.x + j * blockDim.x;
-    if (v < a.nvec) wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
-  }
-  const float static_inv = static_inv_scale<OUT>(a);
-
-  Vec<VEC> xa[VPT], ra[VPT], xb[VPT], rb[VPT];
-  int64_t row = blockIdx.x;
-  if (row < a.rows) persist_load<T, VEC, VPT, RES>(a, row, xa, ra, pol_stream);
-  while (row < a.rows) {
-    int64_t next = row + gridDim.x;
-    if (next < a.rows) persist_load<T, VEC, VPT, RES>(a, next, xb, rb, pol_stream);
-    persist_row<T, VEC, VPT, RES, OUT>(a, row, xa, ra, wv, part[0], amax_part[0], static_inv);
-    row = next;
-    if (row >= a.rows) break;
-    next = row + gridDim.x;
-    if (next < a.rows) persist_load<T, VEC, VPT, RES>(a, next, xa, ra, pol_stream);
-    persist_row<T, VEC, VPT, RES, OUT>(a, row, xb, rb, wv, part[1], amax_part[1], static_inv);
-    row = next;
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Kernel 3: rows longer than the register-resident kernels hold (16-bit
 // output only).  Pass 1 streams the input (and residual) from HBM, writes the
 // rounded residual and sums squares; pass 2 re-reads each thread's own
@@ -602,7 +490,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
 // ---------------------------------------------------------------------------
 // Launch plans.
 
-enum Kind { kWarpRows = 0, kCtaRows = 1, kClusterRows = 2, kTwoPass = 3, kPersist = 4 };
+enum Kind { kWarpRows = 0, kCtaRows = 1, kClusterRows = 2, kTwoPass = 3 };
 
 struct Plan {
   Kind kind = kWarpRows;
@@ -627,7 +515,6 @@ const char* kind_name(Kind k) {
     case kWarpRows: return "warp";
     case kCtaRows: return "cta";
     case kClusterRows: return "cluster";
-    case kPersist: return "persist";
     default: return "twopass";
   }
 }
@@ -642,7 +529,6 @@ std::string plan_string(const Plan& p) {
 // VPT values compiled for each kind and variant (must match the dispatch
 // tables below).
 bool vpt_supported(Kind k, int vec, int vpt, const Variant& v) {
-  if (k == kPersist) return vpt == 1 || vpt == 2 || vpt == 4;
   if (!v.full()) {
     switch (k) {
       case kWarpRows: return vpt == 1 || vpt == 2 || vpt == 4;
@@ -676,11 +562,16 @@ int round_up(int v, int m) { return (v + m - 1) / m * m; }
 //     rows that do fit cost 5-15% (cluster scheduling and the cluster barrier).
 // Without a residual (plain RMSNorm) a thread has half the bytes in flight per
 // vector, and the same sweep run for those forms favours smaller CTAs with
-// more vectors per thread once rows pass 512 vectors: four per thread up to
-// 768 vectors, two beyond (up to 1.23x at hidden 12288 over one per thread).
+// more vectors per thread once rows pass 512 vectors (16-bit output) or 128
+// vectors (fp8 output): up to 1.23x at hidden 12288 over one per thread.
 // Every plan it returns is compiled for every variant, except two passes
 // (rows past 8 * 2048 vectors), which only the 16-bit-output variants have.
-Plan default_plan(int nvec, int vec, bool residual) {
+int plain_vpt(int nvec, bool fp8) {
+  if (fp8) return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : (nvec <= 768 ? 4 : 2));
+  return nvec <= 512 ? 1 : (nvec <= 768 ? 2 : (nvec <= 1024 ? 4 : 2));
+}
+
+Plan default_plan(int nvec, int vec, bool residual, bool fp8) {
   Plan p;
   p.vec = vec;
   if (nvec <= 64) {
@@ -690,9 +581,9 @@ Plan default_plan(int nvec, int vec, bool residual) {
     p.rows_per_cta = residual ? 2 : 4;
     return p;
   }
-  if (!residual && nvec > 512 && nvec <= 2048) {
+  if (!residual && nvec <= 2048) {
     p.kind = kCtaRows;
-    p.vpt = nvec <= 768 ? 4 : 2;
+    p.vpt = plain_vpt(nvec, fp8);
     p.tpr = round_up((nvec + p.vpt - 1) / p.vpt, 32);
     return p;
   }
@@ -742,7 +633,6 @@ bool parse_plan(const std::string& s, Plan* p) {
   else if (k == "cta") p->kind = kCtaRows;
   else if (k == "cluster") p->kind = kClusterRows;
   else if (k == "twopass") p->kind = kTwoPass;
-  else if (k == "persist") p->kind = kPersist;
   else return false;
   p->vec = vec;
   p->vpt = vpt;
@@ -787,14 +677,6 @@ bool plan_valid(const Plan& p, int nvec, int max_vec, const Variant& var, std::s
       }
       return true;
     }
-    case kPersist:
-      if (p.cluster != 1 || p.tpr < 32 || p.tpr > persist_max_threads(p.vpt, var.res) ||
-          p.tpr % 32 || static_cast<int64_t>(p.tpr) * p.vpt < nvec) {
-        *why = "persist plan needs cluster 1, tpr a multiple of 32 within its launch bound and "
-               "tpr * vpt >= vectors per row";
-        return false;
-      }
-      return true;
     default:
       if (p.tpr < 32 || p.tpr > kTwoPassThreads || p.tpr % 32) {
         *why = "twopass tpr must be a multiple of 32 in [32, 512]";
@@ -844,19 +726,8 @@ KernelFn pick_cta(int vpt) {
 }
 
 template <typename T, int VEC, bool RES, int OUT>
-KernelFn pick_persist(int vpt) {
-  switch (vpt) {
-    case 1: return rms_norm_persist_rows<T, VEC, 1, RES, OUT>;
-    case 2: return rms_norm_persist_rows<T, VEC, 2, RES, OUT>;
-    case 4: return rms_norm_persist_rows<T, VEC, 4, RES, OUT>;
-  }
-  return nullptr;
-}
-
-template <typename T, int VEC, bool RES, int OUT>
 KernelFn pick_kind(const Plan& p) {
   switch (p.kind) {
-    case kPersist: return pick_persist<T, VEC, RES, OUT>(p.vpt);
     case kWarpRows: return pick_warp<T, VEC, RES, OUT>(p.vpt);
     case kCtaRows: return pick_cta<T, VEC, false, RES, OUT>(p.vpt);
     case kClusterRows: return pick_cta<T, VEC, true, RES, OUT>(p.vpt);
@@ -1009,15 +880,14 @@ int choose_vec(const Problem& q) {
   return 2;
 }
 
-int make_plan(const Problem& q, Plan* plan, RmsArgs* args) {
-  const Variant var{q.r != nullptr, q.out_form};
+int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   const int max_vec = choose_vec(q);
   if (q.out_form != kOutSame && max_vec < 8)
     return fail(HPRN_ERR_INVALID_ARGUMENT,
                 "fp8 output needs hidden_dim % 4 == 0 and 8-byte aligned input/weight/residual "
                 "rows and 4-byte aligned output rows");
   const int nvec = static_cast<int>(q.hidden / (max_vec / 2));
-  Plan p = default_plan(nvec, max_vec, var.res);
+  Plan p = default_plan(nvec, max_vec, var.res, var.out != kOutSame);
   if (p.kind == kTwoPass && q.out_form != kOutSame)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "rows longer than 16384 vectors are supported with a "
                                            "16-bit output only");
@@ -1054,27 +924,10 @@ int make_plan(const Problem& q, Plan* plan, RmsArgs* args) {
   return HPRN_OK;
 }
 
-// Resident CTAs per SM of `fn` at `threads` threads, cached per device (the
-// persistent kernel's grid is SMs x this).
-int resident_ctas(const DeviceInfo& dev, KernelFn fn, int threads) {
-  static std::mutex mu;
-  static std::map<std::tuple<int, const void*, int>, int> cache;
-  const auto key = std::make_tuple(dev.device, reinterpret_cast<const void*>(fn), threads);
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, 0) != cudaSuccess || n < 1) n = 1;
-  cache[key] = n;
-  return n;
-}
-
-int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const DeviceInfo& dev,
-           cudaStream_t stream, unsigned flags) {
+int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, cudaStream_t stream,
+           unsigned flags) {
   KernelFn fn = pick_kernel(dtype, p, var);
   if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
-  const int64_t persist_grid =
-      p.kind == kPersist ? static_cast<int64_t>(dev.sm_count) * resident_ctas(dev, fn, p.tpr) : 0;
   // Rows handled per CTA-group in grid.x; split very tall problems into launches.
   const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;
   const int64_t ctas_per_unit = p.kind == kClusterRows ? p.cluster : 1;
@@ -1092,9 +945,7 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
     const int64_t units = (n + rows_per_unit - 1) / rows_per_unit;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
-    const int64_t grid = p.kind == kPersist ? (units < persist_grid ? units : persist_grid)
-                                            : units * ctas_per_unit;
-    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.gridDim = dim3(static_cast<unsigned>(units * ctas_per_unit), 1, 1);
     cfg.blockDim = dim3(p.kind == kWarpRows ? 32 * p.rows_per_cta : p.tpr, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
@@ -1129,11 +980,11 @@ int run(const Problem& q, void* stream, unsigned flags) {
   if (q.rows == 0) return ok();
   const DeviceInfo* dev = nullptr;
   if ((st = current_device(&dev)) != HPRN_OK) return st;
+  const Variant var{q.r != nullptr, q.out_form};
   Plan p;
   RmsArgs a;
-  if ((st = make_plan(q, &p, &a)) != HPRN_OK) return st;
-  const Variant var{q.r != nullptr, q.out_form};
-  if ((st = launch(p, a, q.dtype, var, *dev, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK)
+  if ((st = make_plan(q, var, &p, &a)) != HPRN_OK) return st;
+  if ((st = launch(p, a, q.dtype, var, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK)
     return st;
   return ok();
 }
@@ -1187,7 +1038,7 @@ int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* inpu
             nullptr, nullptr};
   Plan p;
   RmsArgs a;
-  const int st = make_plan(q, &p, &a);
+  const int st = make_plan(q, Variant{true, kOutSame}, &p, &a);
   if (st != HPRN_OK) return st;
   snprintf(plan, plan_len, "%s", plan_string(p).c_str());
   return ok();

@@ -55,12 +55,6 @@ def candidates(nvec: int, full: bool = True) -> list[str]:
                 continue
             kind = "cta" if cl == 1 else "cluster"
             out.append(f"{kind}:vec32:vpt{vpt}:tpr{tpr}:cluster{cl}:rpc1")
-    # Persistent CTAs with the next row prefetched (one CTA covers the row).
-    for vpt in (1, 2, 4):
-        tpr = -(-(-(-nvec // vpt)) // 32) * 32
-        if 32 <= tpr <= (1024 if vpt == 1 else 512 if vpt == 2 else 256) and \
-                not (tpr > 32 and (tpr - 32) * vpt >= nvec):
-            out.append(f"persist:vec32:vpt{vpt}:tpr{tpr}:cluster1:rpc1")
     return out
 
 

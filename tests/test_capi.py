@@ -50,6 +50,15 @@ def test_plan_kinds(rows, hidden, kind):
     assert ":vec32:" in p
 
 
+def test_plan_is_for_the_fused_form_whatever_the_pointers():
+    """hprn_rms_norm_plan plans the in-place fused op; a null residual pointer
+    (planning without tensors) must not switch it to the plain form's plans."""
+    assert capi.plan(4096, 16384) == capi.plan(4096, 16384, input_ptr=1 << 20,
+                                               residual_ptr=1 << 21)
+    assert capi.plan(4096, 16384) == "cta:vec32:vpt1:tpr1024:cluster1:rpc1"
+    assert capi.plan(4096, 1024) == "warp:vec32:vpt2:tpr32:cluster1:rpc2"
+
+
 def test_plan_vector_width_follows_alignment_and_hidden():
     assert ":vec32:" in capi.plan(8, 4096, input_ptr=256, residual_ptr=1 << 20)
     assert ":vec16:" in capi.plan(8, 4096, input_ptr=256 + 16, residual_ptr=1 << 20)

@@ -113,12 +113,6 @@ FORCED = [
     (9, 4096, "twopass:vec2:vpt4:tpr512:cluster1:rpc1"),
     (33, 256, "warp:vec16:vpt1:tpr32:cluster1:rpc8"),
     (33, 256, "warp:vec4:vpt4:tpr32:cluster1:rpc3"),
-    (1000, 4096, "persist:vec32:vpt1:tpr256:cluster1:rpc1"),
-    (301, 8192, "persist:vec32:vpt2:tpr256:cluster1:rpc1"),
-    (77, 16384, "persist:vec32:vpt4:tpr256:cluster1:rpc1"),
-    (3, 1024, "persist:vec32:vpt1:tpr64:cluster1:rpc1"),
-    (500, 2048, "persist:vec16:vpt2:tpr128:cluster1:rpc1"),
-    (99, 1024, "persist:vec2:vpt4:tpr256:cluster1:rpc1"),
 ]
 
 

@@ -95,10 +95,6 @@ FORCED = [
     (5, 16384, "cluster:vec32:vpt2:tpr256:cluster2:rpc1"),
     (5, 16384, "cluster:vec32:vpt4:tpr64:cluster4:rpc1"),
     (3, 32768, "cluster:vec32:vpt2:tpr128:cluster8:rpc1"),
-    (700, 4096, "persist:vec32:vpt1:tpr256:cluster1:rpc1"),
-    (301, 8192, "persist:vec32:vpt2:tpr256:cluster1:rpc1"),
-    (77, 16384, "persist:vec32:vpt4:tpr256:cluster1:rpc1"),
-    (150, 2048, "persist:vec16:vpt2:tpr128:cluster1:rpc1"),
 ]
 
 
