@@ -97,10 +97,12 @@ class Dist:
         self.pg = False
 
     def init(self, backend: str):
+        import torch
         import torch.distributed as dist
 
         if self.world > 1 and not dist.is_initialized():
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=180))
+            kw = {"device_id": torch.device("cuda", self.local_rank)} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=180), **kw)
             self.pg = True
 
     def barrier(self):

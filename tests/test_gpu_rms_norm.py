@@ -88,6 +88,18 @@ def test_config1_full_batch_vs_torch_fp32(cuda, hidden):
     torch.testing.assert_close(x.float(), want_out.float(), atol=1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("rows,hidden", [(65536, 8192), (32768, 32768)])
+def test_config4_full_shapes_vs_torch_fp32(cuda, rows, hidden):
+    """BASELINE config 4's global batches at full size on one GPU (the
+    multi-GPU mode runs the same kernel on each rank's block of these rows)."""
+    x, w, r, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=rows, device=cuda)
+    want_out, want_res = torch_fp32_reference(x, w, r, eps)
+    run_capi(x, w, r, eps)
+    assert torch.equal(r.view(torch.int16), want_res.view(torch.int16))
+    assert int(ulp_distance(x, want_out).max()) <= 1
+    del want_out, want_res
+
+
 # Plans forced through the tuning hook: every kernel kind, vector width,
 # vectors-per-thread and cluster size the library compiles.
 FORCED = [
