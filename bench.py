@@ -567,6 +567,8 @@ VARIANTS = {
     "fused_fp8_static": (True, "fp8s", 7),
     "fused_fp8_dynamic": (True, "fp8d", 7),
     "plain_fp8_dynamic": (False, "fp8d", 3),
+    "fused_nvfp4": (True, "nvfp4", 6.5625),   # + e2m1 codes 0.5 B and a scale byte per 16
+    "plain_nvfp4": (False, "nvfp4", 2.5625),
 }
 
 
@@ -594,15 +596,24 @@ def run_variants(args, dist, dev, stream):
             if form == "same":
                 outs = xs if name == "fused_in_place" else \
                     [torch.empty(rows, h, device=dev, dtype=torch.bfloat16) for _ in range(nsets)]
+            elif form == "nvfp4":
+                outs = [torch.empty(rows, h // 2, device=dev, dtype=torch.uint8)
+                        for _ in range(nsets)]
             else:
                 outs = [torch.empty(rows, h, device=dev, dtype=torch.float8_e4m3fn)
                         for _ in range(nsets)]
-            scale = torch.tensor([0.01], device=dev)
+            scale = torch.tensor([0.01 if form != "nvfp4" else 336.0], device=dev)
             rsc = torch.empty(rows, device=dev)
-            ocode = {"same": capi.OUT_SAME, "fp8s": capi.OUT_FP8_E4M3_STATIC,
-                     "fp8d": capi.OUT_FP8_E4M3_DYNAMIC}[form]
+            bsc = torch.empty(rows, h // 16, device=dev, dtype=torch.uint8)
 
-            def call(k, sh, h=h, xs=xs, rs=rs, w=w, outs=outs, ocode=ocode, res=res):
+            def call(k, sh, h=h, xs=xs, rs=rs, w=w, outs=outs, form=form, res=res):
+                if form == "nvfp4":
+                    capi.rms_norm_nvfp4(outs[k].data_ptr(), bsc.data_ptr(), xs[k].data_ptr(),
+                                        w.data_ptr(), rs[k].data_ptr() if res else None, rows, h,
+                                        h, h, h, 1e-6, capi.DTYPE_BF16, scale.data_ptr(), sh)
+                    return
+                ocode = {"same": capi.OUT_SAME, "fp8s": capi.OUT_FP8_E4M3_STATIC,
+                         "fp8d": capi.OUT_FP8_E4M3_DYNAMIC}[form]
                 capi.rms_norm_out(outs[k].data_ptr(), xs[k].data_ptr(), w.data_ptr(),
                                   rs[k].data_ptr() if res else None, rows, h, h, h, h, 1e-6,
                                   capi.DTYPE_BF16, ocode, scale.data_ptr(), rsc.data_ptr(), sh)
@@ -626,7 +637,7 @@ def run_variants(args, dist, dev, stream):
             e1.record()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (3 * L)
-            byt = rows * h * bpe + h * 2 + (rows * 4 if form == "fp8d" else 0)
+            byt = int(rows * h * bpe) + h * 2 + (rows * 4 if form == "fp8d" else 0)
             per.append({"hidden": h, "us": round(us, 2), "gbs": round(byt / us / 1e3, 1),
                         "frac": round(byt / us / 1e3 / peak, 3)})
             del g, xs, rs, outs

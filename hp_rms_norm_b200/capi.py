@@ -32,6 +32,7 @@ ACT_GELU_TANH = 2
 OUT_SAME = 0
 OUT_FP8_E4M3_STATIC = 1
 OUT_FP8_E4M3_DYNAMIC = 2
+OUT_NVFP4 = 3
 
 # Every symbol include/hp_rms_norm_b200.h declares.
 EXPORTED = (
@@ -41,6 +42,7 @@ EXPORTED = (
     "hprn_relu_ex",
     "hprn_rms_norm_out",
     "hprn_act_and_mul",
+    "hprn_rms_norm_nvfp4",
     "hprn_last_error",
     "hprn_status_string",
     "hprn_version",
@@ -83,6 +85,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_rms_norm_out.restype = c_int
     lib.hprn_act_and_mul.argtypes = [vp, vp, i64, i64, i64, i64, c_int, c_int, vp, u32]
     lib.hprn_act_and_mul.restype = c_int
+    lib.hprn_rms_norm_nvfp4.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, i64, i64,
+                                        ctypes.c_double, c_int, vp, vp, u32]
+    lib.hprn_rms_norm_nvfp4.restype = c_int
     lib.hprn_last_error.argtypes = []
     lib.hprn_last_error.restype = ctypes.c_char_p
     lib.hprn_status_string.argtypes = [c_int]
@@ -138,6 +143,16 @@ def rms_norm_out(out_ptr: int, input_ptr: int, weight_ptr: int, residual_ptr: in
     _check(load().hprn_rms_norm_out(out_ptr, input_ptr, weight_ptr, residual_ptr, rows, hidden,
                                     out_row_stride, input_row_stride, residual_row_stride, eps,
                                     dtype, out_form, scale_ptr, row_scales_ptr, stream, flags))
+
+
+def rms_norm_nvfp4(out_ptr: int, block_scales_ptr: int, input_ptr: int, weight_ptr: int,
+                   residual_ptr: int | None, rows: int, hidden: int, out_row_stride: int,
+                   input_row_stride: int, residual_row_stride: int, eps: float, dtype: int,
+                   global_scale_ptr: int, stream: int = 0, flags: int = LAUNCH_DEFAULT) -> None:
+    _check(load().hprn_rms_norm_nvfp4(out_ptr, block_scales_ptr, input_ptr, weight_ptr,
+                                      residual_ptr, rows, hidden, out_row_stride, input_row_stride,
+                                      residual_row_stride, eps, dtype, global_scale_ptr, stream,
+                                      flags))
 
 
 def act_and_mul(out_ptr: int, input_ptr: int, rows: int, d: int, out_row_stride: int,
@@ -230,3 +245,18 @@ def act_and_mul_tensors(out, inp, act: int, stream: int | None = None,
     rows, d = out.shape
     act_and_mul(out.data_ptr(), inp.data_ptr(), rows, d, out.stride(0), inp.stride(0), act,
                 dtype_code(inp), stream, flags)
+
+
+def rms_norm_nvfp4_tensors(out, block_scales, inp, weight, res, eps: float, global_scale,
+                           stream: int | None = None, flags: int = LAUNCH_DEFAULT) -> None:
+    """hprn_rms_norm_nvfp4 on 2-D CUDA tensors: out uint8 [rows, hidden/2] (packed
+    e2m1 pairs), block_scales uint8 / float8_e4m3fn [rows, hidden/16]."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(inp.device).cuda_stream
+    rows, hidden = inp.shape
+    rms_norm_nvfp4(out.data_ptr(), block_scales.data_ptr(), inp.data_ptr(), weight.data_ptr(),
+                   res.data_ptr() if res is not None else None, rows, hidden, out.stride(0) * 2,
+                   inp.stride(0), res.stride(0) if res is not None else hidden, eps,
+                   dtype_code(inp), global_scale.data_ptr(), stream, flags)

@@ -34,6 +34,7 @@
 //     occupancy cliff at large hidden);
 //   * rows too long for the register-resident kernels use a two-pass kernel
 //     that re-reads its own just-written residual from L2, not HBM.
+#include <cuda_fp4.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -52,7 +53,8 @@ namespace hprn {
 enum OutForm : int {
   kOutSame = HPRN_OUT_SAME,                   // 16-bit T into `out` (may be the input)
   kOutFp8Static = HPRN_OUT_FP8_E4M3_STATIC,   // e4m3 with one scale for the tensor
-  kOutFp8Dynamic = HPRN_OUT_FP8_E4M3_DYNAMIC  // e4m3 with one scale per row, written out
+  kOutFp8Dynamic = HPRN_OUT_FP8_E4M3_DYNAMIC,  // e4m3 with one scale per row, written out
+  kOutNvfp4 = HPRN_OUT_NVFP4  // e2m1 pairs + one e4m3 scale per 16 elements (NVFP4)
 };
 
 constexpr float kE4m3Max = 448.0f;
@@ -63,8 +65,9 @@ struct RmsArgs {
   const uint16_t* w;   // weight [hidden]
   uint16_t* r;         // residual rows, updated in place (null: plain RMSNorm)
   void* out;           // output rows (T or e4m3 bytes)
-  const float* scale;  // static fp8 scale (one float)
+  const float* scale;  // static fp8 scale, or the NVFP4 global scale (one float)
   float* row_scales;   // dynamic fp8 scales, one per row
+  uint8_t* block_scales;  // NVFP4 block scales, rows x hidden/16 e4m3 bytes
   int64_t rows;
   int64_t x_stride;    // elements between rows
   int64_t r_stride;
@@ -168,6 +171,44 @@ __device__ __forceinline__ Vec<VEC / 2> quantize_e4m3(const Vec<VEC>& rv, const 
   return o;
 }
 
+// NVFP4 for one 32-byte vector (exactly one 16-element block):
+//   sf = e4m3_satfinite(gs * (max_j |y_j| / 6)),  q_j = e2m1(y_j * (gs / sf))
+// (q = 0 when sf is 0).  Returns the 8 packed bytes (element 2k in the low
+// nibble of byte k) and the scale byte.
+template <typename T>
+__device__ __forceinline__ Vec<8> quantize_nvfp4(const Vec<32>& rv, const Vec<32>& wv, float inv,
+                                                 float gs, uint8_t* sf_out) {
+  float y[16];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float2 a = unpack2<T>(rv.w[k]);
+    const float2 b = unpack2<T>(wv.w[k]);
+    y[2 * k] = a.x * b.x * inv;
+    y[2 * k + 1] = a.y * b.y * inv;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[k]));
+  const __nv_fp8_storage_t sf = __nv_cvt_float_to_fp8(gs * (amax / 6.0f), __NV_SATFINITE, __NV_E4M3);
+  const float sfv = __half2float(__half(__nv_cvt_fp8_to_halfraw(sf, __NV_E4M3)));
+  const float qs = sfv != 0.f ? gs / sfv : 0.f;
+  Vec<8> o;
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int k = 8 * w + 2 * b;
+      const __nv_fp4x2_storage_t p =
+          __nv_cvt_float2_to_fp4x2(make_float2(y[k] * qs, y[k + 1] * qs), __NV_E2M1, cudaRoundNearest);
+      word |= static_cast<uint32_t>(p) << (8 * b);
+    }
+    o.w[w] = word;
+  }
+  *sf_out = sf;
+  return o;
+}
+
 // Butterfly reductions: every lane ends with the same bits.
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -219,10 +260,12 @@ __device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, floa
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
-// Inverse of the static fp8 scale, read after the programmatic-launch wait.
+// Inverse of the static fp8 scale, or the NVFP4 global scale itself, read
+// after the programmatic-launch wait.
 template <int OUT>
 __device__ __forceinline__ float static_inv_scale(const RmsArgs& a) {
   if constexpr (OUT == kOutFp8Static) return 1.0f / __ldg(a.scale);
+  if constexpr (OUT == kOutNvfp4) return __ldg(a.scale);
   return 1.0f;
 }
 
@@ -235,6 +278,13 @@ __device__ __forceinline__ void store_out(const RmsArgs& a, int64_t row, int64_t
   if constexpr (OUT == kOutSame) {
     uint16_t* o = static_cast<uint16_t*>(a.out) + row * a.out_stride + v * EPV;
     st_global<VEC>(o, normalize<T, VEC>(rv, wv, inv));
+  } else if constexpr (OUT == kOutNvfp4) {
+    static_assert(VEC == 32, "NVFP4 blocks are one 32-byte vector of 16 elements");
+    uint8_t sf;
+    // out_stride counts fp4 elements: byte offset = elements / 2.
+    uint8_t* o = static_cast<uint8_t*>(a.out) + (row * a.out_stride + v * EPV) / 2;
+    st_global<8>(o, quantize_nvfp4<T>(rv, wv, inv, inv_scale, &sf));
+    a.block_scales[row * a.nvec + v] = sf;
   } else {
     uint8_t* o = static_cast<uint8_t*>(a.out) + row * a.out_stride + v * EPV;
     st_global<VEC / 2>(o, quantize_e4m3<T, VEC>(rv, wv, inv, inv_scale));
@@ -739,7 +789,9 @@ KernelFn pick_kind(const Plan& p) {
 
 template <typename T, bool RES, int OUT>
 KernelFn pick_vec(const Plan& p) {
-  if constexpr (OUT == kOutSame) {
+  if constexpr (OUT == kOutNvfp4) {
+    return p.vec == 32 ? pick_kind<T, 32, RES, OUT>(p) : nullptr;
+  } else if constexpr (OUT == kOutSame) {
     switch (p.vec) {
       case 32: return pick_kind<T, 32, RES, OUT>(p);
       case 16: return pick_kind<T, 16, RES, OUT>(p);
@@ -763,12 +815,14 @@ KernelFn pick_variant(const Plan& p, const Variant& v) {
     switch (v.out) {
       case kOutSame: return pick_vec<T, true, kOutSame>(p);
       case kOutFp8Static: return pick_vec<T, true, kOutFp8Static>(p);
+      case kOutNvfp4: return pick_vec<T, true, kOutNvfp4>(p);
       default: return pick_vec<T, true, kOutFp8Dynamic>(p);
     }
   }
   switch (v.out) {
     case kOutSame: return pick_vec<T, false, kOutSame>(p);
     case kOutFp8Static: return pick_vec<T, false, kOutFp8Static>(p);
+    case kOutNvfp4: return pick_vec<T, false, kOutNvfp4>(p);
     default: return pick_vec<T, false, kOutFp8Dynamic>(p);
   }
 }
@@ -792,9 +846,12 @@ struct Problem {
   int out_form;
   const float* scale;
   float* row_scales;
+  uint8_t* block_scales;
 };
 
 int out_elem_bytes(const Problem& q) { return q.out_form == kOutSame ? 2 : 1; }
+
+bool is_fp8(const Problem& q) { return q.out_form == kOutFp8Static || q.out_form == kOutFp8Dynamic; }
 
 // [first, last) byte range of `rows` rows of `hidden` elements at `stride`.
 struct Span {
@@ -824,7 +881,8 @@ bool rows_interleave(const void* p, const void* q, int64_t stride_p, int64_t str
 int validate(const Problem& q) {
   if (q.dtype != HPRN_DTYPE_BF16 && q.dtype != HPRN_DTYPE_FP16)
     return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
-  if (q.out_form != kOutSame && q.out_form != kOutFp8Static && q.out_form != kOutFp8Dynamic)
+  if (q.out_form != kOutSame && q.out_form != kOutFp8Static && q.out_form != kOutFp8Dynamic &&
+      q.out_form != kOutNvfp4)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown output form");
   if (q.rows < 0) return fail(HPRN_ERR_INVALID_ARGUMENT, "rows must be >= 0");
   if (q.hidden < 1 || q.hidden > (static_cast<int64_t>(1) << 30))
@@ -835,6 +893,12 @@ int validate(const Problem& q) {
     return fail(HPRN_ERR_INVALID_ARGUMENT, "static fp8 output needs a scale");
   if (q.out_form == kOutFp8Dynamic && !q.row_scales)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "dynamic fp8 output needs a row_scales buffer");
+  if (q.out_form == kOutNvfp4 && (!q.scale || !q.block_scales))
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "NVFP4 output needs a global scale and a block_scales buffer");
+  if (q.out_form == kOutNvfp4 && (q.hidden % 16 || (q.rows > 1 && q.os % 16)))
+    return fail(HPRN_ERR_INVALID_ARGUMENT,
+                "NVFP4 output needs hidden_dim % 16 == 0 and an output row stride that is a "
+                "multiple of 16 elements");
   if (!aligned(q.x, 2) || !aligned(q.w, 2) || (q.r && !aligned(q.r, 2)) ||
       (q.out_form == kOutSame && !aligned(q.out, 2)))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor pointers must be 2-byte aligned");
@@ -842,7 +906,9 @@ int validate(const Problem& q) {
     return fail(HPRN_ERR_INVALID_ARGUMENT, "row strides must be >= hidden_dim");
   const Span xs = span_of(q.x, q.rows, q.hidden, q.xs, 2);
   const Span ws = span_of(q.w, 1, q.hidden, q.hidden, 2);
-  const Span os = span_of(q.out, q.rows, q.hidden, q.os, out_elem_bytes(q));
+  const Span os = q.out_form == kOutNvfp4
+                      ? span_of(q.out, q.rows, q.hidden / 2, q.os / 2, 1)
+                      : span_of(q.out, q.rows, q.hidden, q.os, out_elem_bytes(q));
   // input and residual must not share any element.
   if (q.r) {
     const Span rs = span_of(q.r, q.rows, q.hidden, q.rs, 2);
@@ -865,6 +931,13 @@ int validate(const Problem& q) {
 
 // Largest vector width every pointer, stride and the hidden size allow.
 int choose_vec(const Problem& q) {
+  if (q.out_form == kOutNvfp4) {
+    const bool ok = q.hidden % 16 == 0 && aligned(q.x, 32) && aligned(q.w, 32) &&
+                    (!q.r || aligned(q.r, 32)) && aligned(q.out, 8) &&
+                    (q.rows <= 1 || ((q.xs * 2) % 32 == 0 && (!q.r || (q.rs * 2) % 32 == 0) &&
+                                     (q.os / 2) % 8 == 0));
+    return ok ? 32 : 0;
+  }
   const bool fp8 = q.out_form != kOutSame;
   for (int vec : {32, 16, 8, 4}) {
     const int epv = vec / 2;
@@ -882,7 +955,11 @@ int choose_vec(const Problem& q) {
 
 int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   const int max_vec = choose_vec(q);
-  if (q.out_form != kOutSame && max_vec < 8)
+  if (q.out_form == kOutNvfp4 && max_vec != 32)
+    return fail(HPRN_ERR_INVALID_ARGUMENT,
+                "NVFP4 output needs 32-byte aligned input/weight/residual rows and 8-byte aligned "
+                "output rows");
+  if (is_fp8(q) && max_vec < 8)
     return fail(HPRN_ERR_INVALID_ARGUMENT,
                 "fp8 output needs hidden_dim % 4 == 0 and 8-byte aligned input/weight/residual "
                 "rows and 4-byte aligned output rows");
@@ -910,6 +987,7 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   a.out = q.out;
   a.scale = q.scale;
   a.row_scales = q.row_scales;
+  a.block_scales = q.block_scales;
   a.rows = q.rows;
   a.x_stride = q.xs;
   a.r_stride = q.rs;
@@ -932,15 +1010,19 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, cudaStream_t
   const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;
   const int64_t ctas_per_unit = p.kind == kClusterRows ? p.cluster : 1;
   const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
-  const int out_bytes = var.out == kOutSame ? 2 : 1;
+
   int64_t done = 0;
   while (done < a.rows) {
     RmsArgs c = a;
     const int64_t n = a.rows - done < max_rows ? a.rows - done : max_rows;
     c.x = a.x + done * a.x_stride;
     if (a.r) c.r = a.r + done * a.r_stride;
-    c.out = static_cast<char*>(a.out) + done * a.out_stride * out_bytes;
+    const int64_t out_elems = done * a.out_stride;
+    c.out = static_cast<char*>(a.out) + (var.out == kOutSame    ? out_elems * 2
+                                         : var.out == kOutNvfp4 ? out_elems / 2
+                                                                : out_elems);
     if (a.row_scales) c.row_scales = a.row_scales + done;
+    if (a.block_scales) c.block_scales = a.block_scales + done * a.nvec;
     c.rows = n;
     const int64_t units = (n + rows_per_unit - 1) / rows_per_unit;
     cudaLaunchConfig_t cfg = {};
@@ -1007,7 +1089,7 @@ int hprn_rms_norm_ex(void* input, const void* weight, void* residual, int64_t ro
   if (!residual && rows > 0)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "null tensor pointer (residual)");
   Problem q{input, input, weight, residual, rows, hidden, input_row_stride, input_row_stride,
-            residual_row_stride, eps, dtype, kOutSame, nullptr, nullptr};
+            residual_row_stride, eps, dtype, kOutSame, nullptr, nullptr, nullptr};
   return run(q, stream, flags);
 }
 
@@ -1017,8 +1099,20 @@ int hprn_rms_norm_out(void* out, const void* input, const void* weight, void* re
                       int dtype, int out_form, const float* scale, float* row_scales,
                       void* stream, unsigned flags) {
   using namespace hprn;
+  if (out_form == HPRN_OUT_NVFP4)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "NVFP4 output goes through hprn_rms_norm_nvfp4");
   Problem q{out, input, weight, residual, rows, hidden, out_row_stride, input_row_stride,
-            residual_row_stride, eps, dtype, out_form, scale, row_scales};
+            residual_row_stride, eps, dtype, out_form, scale, row_scales, nullptr};
+  return run(q, stream, flags);
+}
+
+int hprn_rms_norm_nvfp4(void* out, uint8_t* block_scales, const void* input, const void* weight,
+                        void* residual, int64_t rows, int64_t hidden, int64_t out_row_stride,
+                        int64_t input_row_stride, int64_t residual_row_stride, double eps,
+                        int dtype, const float* global_scale, void* stream, unsigned flags) {
+  using namespace hprn;
+  Problem q{out, input, weight, residual, rows, hidden, out_row_stride, input_row_stride,
+            residual_row_stride, eps, dtype, kOutNvfp4, global_scale, nullptr, block_scales};
   return run(q, stream, flags);
 }
 
@@ -1035,7 +1129,7 @@ int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* inpu
   void* x = const_cast<void*>(input);
   Problem q{x, input, input, const_cast<void*>(residual), rows < 1 ? 1 : rows, hidden,
             input_row_stride, input_row_stride, residual_row_stride, 1e-6, dtype, kOutSame,
-            nullptr, nullptr};
+            nullptr, nullptr, nullptr};
   Plan p;
   RmsArgs a;
   const int st = make_plan(q, Variant{true, kOutSame}, &p, &a);

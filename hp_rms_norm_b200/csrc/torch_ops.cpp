@@ -211,6 +211,60 @@ void rms_norm_fp8(at::Tensor& out, const at::Tensor& input, const at::Tensor& we
                                  rsp, stream, HPRN_LAUNCH_DEFAULT));
 }
 
+// NVFP4 output (extension past the reference): out uint8 [..., hidden/2] holds
+// e2m1 pairs (element 2k in the low nibble), block_scales (uint8 or
+// float8_e4m3fn) [..., hidden/16] one e4m3 scale per 16 elements, global_scale
+// one float32: y ~ e2m1 * scale / global_scale.
+void rms_norm_nvfp4(at::Tensor& out, at::Tensor& block_scales, const at::Tensor& input,
+                    const at::Tensor& weight, c10::optional<at::Tensor> residual, double eps,
+                    const at::Tensor& global_scale) {
+  TORCH_CHECK(input.dim() >= 1 && weight.dim() == 1 && input.size(-1) == weight.size(0),
+              "input.size(-1) == hidden_dim");
+  const int64_t hidden = weight.size(0);
+  TORCH_CHECK(hidden % 16 == 0, "NVFP4 output needs hidden_dim % 16 == 0");
+  TORCH_CHECK(out.scalar_type() == at::kByte, "out must be uint8 (two e2m1 codes per byte)");
+  TORCH_CHECK(block_scales.scalar_type() == at::kByte ||
+                  block_scales.scalar_type() == at::kFloat8_e4m3fn,
+              "block_scales must be uint8 or float8_e4m3fn");
+  TORCH_CHECK(out.dim() == input.dim() && block_scales.dim() == input.dim(),
+              "out and block_scales must have the input's rank");
+  for (int64_t i = 0; i + 1 < input.dim(); ++i)
+    TORCH_CHECK(out.size(i) == input.size(i) && block_scales.size(i) == input.size(i),
+                "out and block_scales must agree with the input on leading dimensions");
+  TORCH_CHECK(out.size(-1) == hidden / 2 && block_scales.size(-1) == hidden / 16,
+              "out.size(-1) == hidden_dim / 2 and block_scales.size(-1) == hidden_dim / 16");
+  TORCH_CHECK(block_scales.is_contiguous(), "block_scales must be contiguous");
+  TORCH_CHECK(global_scale.scalar_type() == at::kFloat && global_scale.numel() == 1,
+              "global_scale must be one float32");
+  const at::Tensor* all[] = {&out, &block_scales, &input, &weight, &global_scale};
+  for (const at::Tensor* t : all)
+    TORCH_CHECK(t->is_cuda() && t->device() == input.device(), "tensors must share a CUDA device");
+  TORCH_CHECK(weight.scalar_type() == input.scalar_type(), "input and weight must have the same dtype");
+  TORCH_CHECK(input.stride(-1) == 1 && out.stride(-1) == 1 && weight.stride(0) == 1,
+              "input, out and weight must be contiguous in the last dimension");
+  const int dtype = dtype_code(input);
+  int64_t rows = 0, xs = 0, orows = 0, os = 0, rs = hidden;
+  rows_of(input, "input", &rows, &xs);
+  rows_of(out, "out", &orows, &os);
+  void* rp = nullptr;
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->sizes() == input.sizes() && residual->scalar_type() == input.scalar_type() &&
+                    residual->is_cuda() && residual->device() == input.device() &&
+                    residual->stride(-1) == 1,
+                "residual must match the input's shape, dtype and device");
+    int64_t rrows = 0;
+    rows_of(*residual, "residual", &rrows, &rs);
+    rp = residual->data_ptr();
+  }
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_rms_norm_nvfp4(out.data_ptr(), static_cast<uint8_t*>(block_scales.data_ptr()),
+                                   input.data_ptr(), weight.data_ptr(), rp, rows, hidden, os * 2,
+                                   xs, rs, eps, dtype, global_scale.data_ptr<float>(), stream,
+                                   HPRN_LAUNCH_DEFAULT));
+}
+
 // out[..., d] = act(input[..., :d]) * input[..., d:]  (extension past the reference).
 void act_and_mul(at::Tensor& out, const at::Tensor& input, int act) {
   TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 2 == 0, "input.size(-1) must be even");
@@ -251,6 +305,8 @@ void rms_norm_fp8_meta(at::Tensor&, const at::Tensor&, const at::Tensor&,
                        c10::optional<at::Tensor>, double, c10::optional<at::Tensor>,
                        c10::optional<at::Tensor>) {}
 void act_and_mul_meta(at::Tensor&, const at::Tensor&) {}
+void rms_norm_nvfp4_meta(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&,
+                         c10::optional<at::Tensor>, double, const at::Tensor&) {}
 
 }  // namespace
 
@@ -263,6 +319,8 @@ TORCH_LIBRARY(hp_rms_norm, m) {
         "float eps) -> ()");
   m.def("rms_norm_fp8(Tensor(a!) out, Tensor input, Tensor weight, Tensor(b!)? residual, "
         "float eps, Tensor? scale, Tensor(c!)? row_scales) -> ()");
+  m.def("rms_norm_nvfp4(Tensor(a!) out, Tensor(b!) block_scales, Tensor input, Tensor weight, "
+        "Tensor(c!)? residual, float eps, Tensor global_scale) -> ()");
   // Extensions: gated activations.
   m.def("silu_and_mul(Tensor(a!) out, Tensor input) -> ()");
   m.def("gelu_and_mul(Tensor(a!) out, Tensor input) -> ()");
@@ -274,6 +332,7 @@ TORCH_LIBRARY_IMPL(hp_rms_norm, CUDA, m) {
   m.impl("relu", &relu);
   m.impl("rms_norm_out", &rms_norm_out);
   m.impl("rms_norm_fp8", &rms_norm_fp8);
+  m.impl("rms_norm_nvfp4", &rms_norm_nvfp4);
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("gelu_and_mul", &gelu_and_mul);
   m.impl("gelu_tanh_and_mul", &gelu_tanh_and_mul);
@@ -284,6 +343,7 @@ TORCH_LIBRARY_IMPL(hp_rms_norm, Meta, m) {
   m.impl("relu", &relu_meta);
   m.impl("rms_norm_out", &rms_norm_out_meta);
   m.impl("rms_norm_fp8", &rms_norm_fp8_meta);
+  m.impl("rms_norm_nvfp4", &rms_norm_nvfp4_meta);
   m.impl("silu_and_mul", &act_and_mul_meta);
   m.impl("gelu_and_mul", &act_and_mul_meta);
   m.impl("gelu_tanh_and_mul", &act_and_mul_meta);

@@ -9,7 +9,7 @@ and returns None; ``relu(output, input)`` writes ``torch.relu(input)`` into
 Extensions (not in the reference): ``rms_norm`` (plain RMSNorm),
 ``fused_add_rms_norm`` (the fused op into a separate output) and
 ``rms_norm_fp8`` (either form with an fp8 e4m3 output, static or per-row
-scale), and the gated activations ``silu_and_mul``, ``gelu_and_mul`` and
+scale), ``rms_norm_nvfp4`` (NVFP4 output), and the gated activations ``silu_and_mul``, ``gelu_and_mul`` and
 ``gelu_tanh_and_mul``.  Everything dispatches through ``torch.ops.hp_rms_norm``, registered
 by this package's compiled ``_C`` extension.
 """
@@ -66,6 +66,22 @@ def rms_norm_fp8(input, weight, eps, residual=None, scale=None, out=None):
     return out, row_scales
 
 
+def rms_norm_nvfp4(input, weight, eps, global_scale, residual=None):
+    """RMSNorm (fused with ``residual += input`` when a residual is given) with
+    an NVFP4 output: returns (codes, block_scales), codes uint8
+    [..., hidden/2] holding two e2m1 values per byte (element 2k in the low
+    nibble), block_scales float8_e4m3fn [..., hidden/16]; the normalised value
+    is approximately e2m1 * block_scale / global_scale (``global_scale`` a
+    one-element float32 tensor)."""
+    h = input.shape[-1]
+    codes = torch.empty(input.shape[:-1] + (h // 2,), dtype=torch.uint8, device=input.device)
+    scales = torch.empty(input.shape[:-1] + (h // 16,), dtype=torch.float8_e4m3fn,
+                         device=input.device)
+    torch.ops.hp_rms_norm.rms_norm_nvfp4.default(codes, scales, input, weight, residual, eps,
+                                                 global_scale)
+    return codes, scales
+
+
 def _act_and_mul(op, input, out):
     if out is None:
         out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), dtype=input.dtype,
@@ -89,5 +105,5 @@ def gelu_tanh_and_mul(input, out=None):
     return _act_and_mul(torch.ops.hp_rms_norm.gelu_tanh_and_mul.default, input, out)
 
 
-__all__ = ["hp_rms_norm", "relu", "rms_norm", "fused_add_rms_norm", "rms_norm_fp8",
+__all__ = ["hp_rms_norm", "relu", "rms_norm", "fused_add_rms_norm", "rms_norm_fp8", "rms_norm_nvfp4",
            "silu_and_mul", "gelu_and_mul", "gelu_tanh_and_mul", "torch"]

@@ -56,7 +56,8 @@ typedef enum hprn_dtype {
 typedef enum hprn_out_form {
   HPRN_OUT_SAME = 0,              /* 16-bit, the input's dtype */
   HPRN_OUT_FP8_E4M3_STATIC = 1,   /* fp8 e4m3 (OCP E4M3FN), one scale for the tensor */
-  HPRN_OUT_FP8_E4M3_DYNAMIC = 2   /* fp8 e4m3, one scale per row, written to row_scales */
+  HPRN_OUT_FP8_E4M3_DYNAMIC = 2,  /* fp8 e4m3, one scale per row, written to row_scales */
+  HPRN_OUT_NVFP4 = 3              /* fp4 e2m1 + e4m3 block scales: hprn_rms_norm_nvfp4 only */
 } hprn_out_form;
 
 /* Activations of hprn_act_and_mul. */
@@ -163,6 +164,23 @@ HPRN_API int hprn_rms_norm_out(void* out, const void* input, const void* weight,
 HPRN_API int hprn_act_and_mul(void* out, const void* input, int64_t rows, int64_t d,
                               int64_t out_row_stride, int64_t input_row_stride, int act,
                               int dtype, void* stream, unsigned flags);
+
+/*
+ * The same row operation as hprn_rms_norm_out (residual optional) with an
+ * NVFP4 output (an extension past the reference): for every 16-element block
+ * b of a row, with gs = *global_scale (one float on the device),
+ *   block_scales[i, b] = sf = e4m3_satfinite(gs * (max_j |y_ij| / 6))
+ *   q_ij = e2m1_satfinite(y_ij * (gs / sf))     (0 when sf == 0; NaN -> +6)
+ * so y ~ q * sf / gs.  `out` holds two e2m1 codes per byte, element 2k in the
+ * low nibble; out_row_stride counts fp4 elements (a multiple of 16).
+ * block_scales is rows x hidden/16 bytes, row-major.  Needs hidden % 16 == 0,
+ * 32-byte aligned input/weight/residual rows and 8-byte aligned output rows.
+ */
+HPRN_API int hprn_rms_norm_nvfp4(void* out, uint8_t* block_scales, const void* input,
+                                 const void* weight, void* residual, int64_t rows, int64_t hidden,
+                                 int64_t out_row_stride, int64_t input_row_stride,
+                                 int64_t residual_row_stride, double eps, int dtype,
+                                 const float* global_scale, void* stream, unsigned flags);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 HPRN_API const char* hprn_last_error(void);

@@ -57,6 +57,11 @@ def _load():
         lib.oracle_f32_to_e4m3.restype = None
         lib.oracle_act_and_mul.argtypes = [ctypes.c_int, ctypes.c_int, u16p, u16p, i64, i64]
         lib.oracle_act_and_mul.restype = None
+        lib.oracle_f32_to_e2m1.argtypes = [vp, vp, i64]
+        lib.oracle_f32_to_e2m1.restype = None
+        lib.oracle_rms_norm_nvfp4.argtypes = [ctypes.c_int, vp, vp, u16p, u16p, vp, i64, i64,
+                                              ctypes.c_double, ctypes.c_float]
+        lib.oracle_rms_norm_nvfp4.restype = None
         _lib = lib
     return _lib
 
@@ -118,6 +123,32 @@ def f32_to_e4m3(vals: np.ndarray) -> np.ndarray:
     out = np.empty(v.shape, dtype=np.uint8)
     lib.oracle_f32_to_e4m3(v.ctypes.data, out.ctypes.data, v.size)
     return out
+
+
+def f32_to_e2m1(vals: np.ndarray) -> np.ndarray:
+    lib = _load()
+    v = np.ascontiguousarray(vals, dtype=np.float32)
+    out = np.empty(v.shape, dtype=np.uint8)
+    lib.oracle_f32_to_e2m1(v.ctypes.data, out.ctypes.data, v.size)
+    return out
+
+
+def rms_norm_nvfp4(dtype: int, x: np.ndarray, w: np.ndarray, eps: float, global_scale: float,
+                   r: np.ndarray | None = None):
+    """NVFP4 output of the row op: returns (packed fp4 [rows, hidden/2] uint8,
+    block scales [rows, hidden/16] e4m3 bytes, residual or None)."""
+    lib = _load()
+    hidden = x.shape[-1]
+    xc = np.ascontiguousarray(x, dtype=np.uint16)
+    rows = xc.size // hidden
+    rc = None if r is None else np.ascontiguousarray(r, dtype=np.uint16).copy()
+    out = np.empty((rows, hidden // 2), dtype=np.uint8)
+    sf = np.empty((rows, hidden // 16), dtype=np.uint8)
+    lib.oracle_rms_norm_nvfp4(dtype, out.ctypes.data, sf.ctypes.data, _u16(xc),
+                              _u16(np.ascontiguousarray(w, dtype=np.uint16)),
+                              None if rc is None else rc.ctypes.data, rows, hidden, float(eps),
+                              float(global_scale))
+    return out, sf, rc
 
 
 ACTS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}

@@ -230,6 +230,80 @@ void oracle_rms_norm_out(int dtype, void* out, const uint16_t* input, const uint
   }
 }
 
+/* ---- fp4 e2m1 (values 0, 0.5, 1, 1.5, 2, 3, 4, 6; no inf/NaN) -------------
+ * Round to nearest even, saturating to +-6, from the format definition:
+ * sign bit 3, two exponent bits (bias 1), one mantissa bit; exponent 0 is the
+ * subnormal 0.5 step. */
+static uint8_t f32_to_e2m1_satfinite(float f) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  uint8_t sign = signbit(f) ? 0x8 : 0x0;
+  float a = fabsf(f);
+  if (a != a) return 0x7; /* NaN: positive maximum, as the GPU conversion does */
+  if (a >= 6.0f) return (uint8_t)(sign | 0x7);
+  int best = 0;
+  for (int c = 1; c < 8; ++c) {
+    float dc = fabsf(a - mag[c]), db = fabsf(a - mag[best]);
+    if (dc < db || (dc == db && (c & 1) == 0 && (best & 1) == 1)) best = c;
+  }
+  return (uint8_t)(sign | best);
+}
+
+void oracle_f32_to_e2m1(const float* in, uint8_t* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = f32_to_e2m1_satfinite(in[i]);
+}
+
+/*
+ * NVFP4 output of the row op (an extension past the reference): y as in
+ * oracle_rms_norm_out; for each 16-element block b of a row,
+ *   sf_b  = e4m3_satfinite(gs * (max_j |y_j| / 6))         (stored, one byte)
+ *   q_j   = e2m1_satfinite(y_j * (gs / float(sf_b)))   (0 when sf_b is 0)
+ * two codes per byte, element 2k in the low nibble.  gs is the per-tensor
+ * global scale.  out: rows x hidden/2 bytes; block_scales: rows x hidden/16.
+ */
+void oracle_rms_norm_nvfp4(int dtype, uint8_t* out, uint8_t* block_scales, const uint16_t* input,
+                           const uint16_t* weight, uint16_t* residual, int64_t rows,
+                           int64_t hidden, double eps, float gs) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    const uint16_t* x = input + i * hidden;
+    uint16_t* r = residual ? residual + i * hidden : 0;
+    double ss = 0.0;
+    float* y = (float*)malloc(sizeof(float) * (size_t)hidden);
+    for (int64_t j = 0; j < hidden; ++j) {
+      float s = to_f32(dtype, x[j]);
+      if (r) {
+        s = s + to_f32(dtype, r[j]);
+        r[j] = from_f32(dtype, s);
+        y[j] = to_f32(dtype, r[j]);
+      } else {
+        y[j] = s;
+      }
+      ss += (double)s * (double)s;
+    }
+    float inv = (float)(1.0 / sqrt(ss / (double)hidden + eps));
+    for (int64_t j = 0; j < hidden; ++j) y[j] = y[j] * to_f32(dtype, weight[j]) * inv;
+    for (int64_t b = 0; b < hidden / 16; ++b) {
+      float amax = 0.0f;
+      for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[b * 16 + k]));
+      uint8_t sf = f32_to_e4m3_satfinite(gs * (amax / 6.0f));
+      block_scales[i * (hidden / 16) + b] = sf;
+      float sfv = 0.0f;
+      {
+        /* exact value of the e4m3 code */
+        int e = (sf >> 3) & 0xf, m = sf & 0x7;
+        sfv = e == 0 ? ldexpf((float)m, -9) : ldexpf(1.0f + (float)m / 8.0f, e - 7);
+      }
+      float qs = sfv != 0.0f ? gs / sfv : 0.0f;
+      for (int k = 0; k < 16; k += 2) {
+        uint8_t lo = f32_to_e2m1_satfinite(y[b * 16 + k] * qs);
+        uint8_t hi = f32_to_e2m1_satfinite(y[b * 16 + k + 1] * qs);
+        out[i * (hidden / 2) + (b * 16 + k) / 2] = (uint8_t)(lo | (hi << 4));
+      }
+    }
+    free(y);
+  }
+}
+
 /* torch.relu (CUDA) on raw 16-bit patterns: every value <= 0 (negatives, -inf,
  * -0.0) becomes +0; NaNs and positives pass through unchanged. */
 void oracle_relu(int dtype, uint16_t* out, const uint16_t* in, int64_t n) {

@@ -70,3 +70,36 @@ def test_fp8_dynamic_scales():
     deq = torch.from_numpy(q.view(np.int8)).view(torch.float8_e4m3fn).float().numpy()
     assert np.abs(deq).max() <= 448.0
     assert (np.abs(deq).max(axis=1) >= 416.0).all()  # every row reaches the top of the range
+
+
+def test_e2m1_conversion_table():
+    """e2m1 (NVFP4 element): round to nearest even over {0, .5, 1, 1.5, 2, 3, 4, 6},
+    saturating at 6; NaN -> +6 (code 7), the GPU conversion's rule."""
+    vals = np.array([0.0, -0.0, 0.25, 0.2501, 0.75, 1.25, 1.7, 1.75, 2.5, 2.51, 3.5, 5.0, 5.01,
+                     6.0, 7.0, 1e9, -0.3, -2.5, -100.0, np.nan], dtype=np.float32)
+    want = [0x0, 0x8, 0x0, 0x1, 0x2, 0x2, 0x3, 0x4, 0x4, 0x5, 0x6, 0x6, 0x7,
+            0x7, 0x7, 0x7, 0x9, 0xC, 0xF, 0x7]
+    assert list(O.f32_to_e2m1(vals)) == want
+
+
+@pytest.mark.parametrize("residual", [False, True])
+def test_nvfp4_dequantises_within_half_a_step(residual):
+    code = O.BF16
+    x, w, r = _inputs(11, 4096, code, 5)
+    gs = 448.0 * 6.0 / 8.0
+    q, sf, res = O.rms_norm_nvfp4(code, x, w, 1e-6, gs, r=r if residual else None)
+    y16, res16, _ = O.rms_norm_out(code, x, w, 1e-6, r=r if residual else None)
+    if residual:
+        assert (res == res16).all()
+    mag = np.array([0, 0.5, 1, 1.5, 2, 3, 4, 6], dtype=np.float32)
+    lo, hi = q & 0xF, q >> 4
+    codes = np.stack([lo, hi], axis=-1).reshape(11, 4096)
+    vals = np.where(codes & 8, -1.0, 1.0) * mag[codes & 7]
+    sfv = torch.from_numpy(sf.view(np.int8)).view(torch.float8_e4m3fn).float().numpy()
+    deq = vals.reshape(11, 256, 16) * (sfv / gs)[..., None]
+    y = O.to_f32(code, y16).reshape(11, 256, 16)
+    # half of the widest e2m1 step (4 -> 6) in each block's units, plus bf16 rounding of y
+    bound = (sfv / gs)[..., None] * 1.0 + np.abs(y) * 2 ** -8
+    assert np.all(np.abs(deq - y) <= bound)
+    amax = np.abs(y).max(axis=-1)
+    np.testing.assert_allclose(sfv, gs * amax / 6.0, rtol=2 ** -3)
