@@ -291,6 +291,20 @@ __device__ __forceinline__ void store_out(const RmsArgs& a, int64_t row, int64_t
   }
 }
 
+// The weight vector for output vector v.  With a residual, the weight was
+// loaded before the reduction (its latency hides behind the barrier) and is
+// passed in; without one, it is loaded here, at use: a plain row holds half
+// the bytes per thread, so keeping the weight out of the registers live
+// across the barrier lets more CTAs reside per SM (at hidden 24576, two
+// 768-thread CTAs instead of one), which is what a plain row's bandwidth
+// depends on.
+template <int VEC, bool RES>
+__device__ __forceinline__ Vec<VEC> weight_vec(const RmsArgs& a, int64_t v, const Vec<VEC>& held,
+                                               uint64_t pol_keep) {
+  if constexpr (RES) return held;
+  return ld_weight<VEC>(a.w + v * Vec<VEC>::kElems, pol_keep);
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 1: one warp per row (rows of at most 4 * 32 vectors).  No shared
 // memory, no block barrier: a warp that has finished its row retires without
@@ -327,7 +341,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
       } else {
         square_sum<T, VEC>(xv[j], a0, a1);
       }
-      wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
+      if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
     }
   }
   const float inv = rsqrtf(fmaf(warp_sum(a0 + a1), a.inv_hidden, a.eps));
@@ -335,8 +349,10 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   if constexpr (OUT == kOutFp8Dynamic) {
     float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < VPT; ++j)
-      if (lane + 32 * j < a.nvec) m = vec_amax<T, VEC>(xv[j], wv[j], inv, m);
+    for (int j = 0; j < VPT; ++j) {
+      const int v = lane + 32 * j;
+      if (v < a.nvec) m = vec_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv, m);
+    }
     const float scale = fmaxf(warp_max(m), kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
     if (lane == 0) a.row_scales[row] = scale;
@@ -344,7 +360,9 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = lane + 32 * j;
-    if (v < a.nvec) store_out<T, VEC, OUT>(a, row, v, xv[j], wv[j], inv, inv_scale);
+    if (v < a.nvec)
+      store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
+                             inv_scale);
   }
 }
 
@@ -416,7 +434,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
       } else {
         square_sum<T, VEC>(xv[j], a0, a1);
       }
-      wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
+      if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
     }
   }
 
@@ -437,8 +455,10 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   if constexpr (OUT == kOutFp8Dynamic) {
     float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < VPT; ++j)
-      if (v_begin + tid + j * nthreads < v_end) m = vec_amax<T, VEC>(xv[j], wv[j], inv, m);
+    for (int j = 0; j < VPT; ++j) {
+      const int v = v_begin + tid + j * nthreads;
+      if (v < v_end) m = vec_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv, m);
+    }
     m = warp_max(m);
     if (lane == 0) warp_amax[warp] = m;
     __syncthreads();
@@ -456,7 +476,9 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = v_begin + tid + j * nthreads;
-    if (v < v_end) store_out<T, VEC, OUT>(a, row, v, xv[j], wv[j], inv, inv_scale);
+    if (v < v_end)
+      store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
+                             inv_scale);
   }
 }
 
@@ -610,30 +632,38 @@ int round_up(int v, int m) { return (v + m - 1) / m * m; }
 //     vectors, where 1024-thread CTAs would leave SMs a CTA short);
 //   * thread-block clusters only once a row no longer fits one CTA: splitting
 //     rows that do fit cost 5-15% (cluster scheduling and the cluster barrier).
-// Without a residual (plain RMSNorm) a thread has half the bytes in flight per
-// vector, and the same sweep run for those forms favours smaller CTAs with
-// more vectors per thread once rows pass 512 vectors (16-bit output) or 128
-// vectors (fp8 output): up to 1.23x at hidden 12288 over one per thread.
-// Every plan it returns is compiled for every variant, except two passes
-// (rows past 8 * 2048 vectors), which only the 16-bit-output variants have.
-int plain_vpt(int nvec, bool fp8) {
-  if (fp8) return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : (nvec <= 768 ? 4 : 2));
-  return nvec <= 512 ? 1 : (nvec <= 768 ? 2 : (nvec <= 1024 ? 4 : 2));
+// The extended forms (plain rows, quantised outputs) hold more live values per
+// vector in their epilogues, or half the bytes per vector in flight (no
+// residual), and the same sweep run per form (tune.py --variant) favours more
+// vectors per thread in smaller CTAs as rows grow.  Vectors per thread for a
+// one-CTA row of nvec vectors, or 0 for the warp-per-row kernel:
+int extended_vpt(int nvec, bool residual, int out) {
+  if (residual) return out == kOutNvfp4 ? (nvec <= 256 ? 1 : 2) : -1;  // -1: the fused rule
+  if (nvec <= 64) return 0;
+  switch (out) {
+    case kOutSame: return nvec <= 128 ? 0 : (nvec <= 256 ? 1 : 2);
+    case kOutFp8Static: return nvec <= 128 ? 0 : (nvec <= 1024 ? 2 : 4);
+    case kOutFp8Dynamic: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
+    default: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : (nvec <= 1536 ? 4 : 2));  // NVFP4
+  }
 }
 
-Plan default_plan(int nvec, int vec, bool residual, bool fp8) {
+// Every plan default_plan returns is compiled for every variant, except two
+// passes (rows past 8 * 2048 vectors), which only the 16-bit outputs have.
+Plan default_plan(int nvec, int vec, bool residual, int out) {
   Plan p;
   p.vec = vec;
-  if (nvec <= 64) {
+  const int ext = nvec <= 2048 ? extended_vpt(nvec, residual, out) : -1;
+  if (nvec <= 64 || ext == 0) {
     p.kind = kWarpRows;
-    p.vpt = (nvec + 31) / 32;
+    p.vpt = nvec <= 64 ? (nvec + 31) / 32 : 4;
     p.tpr = 32;
     p.rows_per_cta = residual ? 2 : 4;
     return p;
   }
-  if (!residual && nvec <= 2048) {
+  if (ext > 0) {
     p.kind = kCtaRows;
-    p.vpt = plain_vpt(nvec, fp8);
+    p.vpt = ext;
     p.tpr = round_up((nvec + p.vpt - 1) / p.vpt, 32);
     return p;
   }
@@ -964,7 +994,7 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
                 "fp8 output needs hidden_dim % 4 == 0 and 8-byte aligned input/weight/residual "
                 "rows and 4-byte aligned output rows");
   const int nvec = static_cast<int>(q.hidden / (max_vec / 2));
-  Plan p = default_plan(nvec, max_vec, var.res, var.out != kOutSame);
+  Plan p = default_plan(nvec, max_vec, var.res, var.out);
   if (p.kind == kTwoPass && q.out_form != kOutSame)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "rows longer than 16384 vectors are supported with a "
                                            "16-bit output only");

@@ -32,6 +32,8 @@ VARIANTS = {
     "fused_fp8d": (True, "fp8d", 7),
     "plain_fp8s": (False, "fp8s", 3),
     "plain_fp8d": (False, "fp8d", 3),
+    "fused_nvfp4": (True, "nvfp4", 6.5625),
+    "plain_nvfp4": (False, "nvfp4", 2.5625),
 }
 
 
@@ -88,7 +90,7 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
 
     res_needed, form_name, bpe = VARIANTS[variant]
     form = {"same": capi.OUT_SAME, "fp8s": capi.OUT_FP8_E4M3_STATIC,
-            "fp8d": capi.OUT_FP8_E4M3_DYNAMIC}[form_name]
+            "fp8d": capi.OUT_FP8_E4M3_DYNAMIC, "nvfp4": capi.OUT_NVFP4}[form_name]
 
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     code = capi.DTYPE_BF16 if dtype == "bf16" else capi.DTYPE_FP16
@@ -103,14 +105,22 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
         fp8 = form != capi.OUT_SAME
         if variant == "fused":
             outs = xs
+        elif form == capi.OUT_NVFP4:
+            outs = [torch.empty(rows, h // 2, device=dev, dtype=torch.uint8) for _ in range(nsets)]
         else:
             outs = [torch.empty(rows, h, device=dev,
                                 dtype=torch.float8_e4m3fn if fp8 else tdt) for _ in range(nsets)]
-        scale = torch.tensor([0.01], device=dev)
+        scale = torch.tensor([0.01 if form != capi.OUT_NVFP4 else 336.0], device=dev)
         row_scales = torch.empty(rows, device=dev)
-        byt = rows * h * bpe + 2 * h + (4 * rows if form_name == "fp8d" else 0)
+        block_scales = torch.empty(rows, max(1, h // 16), device=dev, dtype=torch.uint8)
+        byt = int(rows * h * bpe) + 2 * h + (4 * rows if form_name == "fp8d" else 0)
 
         def run(k, s):
+            if form == capi.OUT_NVFP4:
+                capi.rms_norm_nvfp4(outs[k].data_ptr(), block_scales.data_ptr(), xs[k].data_ptr(),
+                                    w.data_ptr(), rs[k].data_ptr() if res_needed else None, rows,
+                                    h, h, h, h, 1e-6, code, scale.data_ptr(), s)
+                return
             capi.rms_norm_out(outs[k].data_ptr(), xs[k].data_ptr(), w.data_ptr(),
                               rs[k].data_ptr() if res_needed else None, rows, h, h, h, h, 1e-6,
                               code, form, scale.data_ptr(), row_scales.data_ptr(), s)
