@@ -30,12 +30,15 @@ LIB = os.path.join(PKG, LIB_NAME)
 CUDA_SOURCES = ["rms_norm.cu", "relu.cu", "act_and_mul.cu", "runtime.cu"]
 HEADERS = ["vec.cuh", "runtime.cuh"]
 
+# HPRN_DEBUG=1 builds host code without optimisation and with debug symbols
+# (device code keeps -O3 and -lineinfo, so kernels stay representative).
+DEBUG = os.environ.get("HPRN_DEBUG", "0") == "1"
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "-Xptxas", "-v",
-]
+] + (["-Xcompiler", "-O0", "-Xcompiler", "-g"] if DEBUG else [])
 
 
 def ext_path() -> str:
@@ -98,8 +101,11 @@ def build_torch_binding(force: bool = False) -> str:
                                             sysconfig.get_paths()["include"]]
     libdirs = cpp_extension.library_paths()
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
-    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+    cmd = ["g++", "-O0" if DEBUG else "-O2", "-std=c++17", "-shared", "-fPIC",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
            "-DTORCH_EXTENSION_NAME=_C"]
+    if DEBUG:
+        cmd.append("-g")
     cmd += [f"-I{d}" for d in incs]
     cmd += [src, "-o", out, f"-L{PKG}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN"]
     for d in libdirs:

@@ -42,6 +42,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+#include <mutex>
 #include <string>
 
 #include "runtime.cuh"
@@ -698,9 +700,34 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
   return p;
 }
 
-// Optional plan override for benchmarking and tuning (hprn_set_plan_override).
-std::string g_override;
-bool g_override_set = false;
+bool parse_plan(const std::string& s, Plan* p);
+
+// Optional plan override for benchmarking and tuning: hprn_set_plan_override,
+// or the HP_RMS_NORM_PLAN environment variable (read at the first call).
+// Parsed once when set; calls read it under a mutex only while one is set.
+std::mutex g_override_mu;
+std::atomic<bool> g_override_set{false};
+Plan g_override_plan;
+std::once_flag g_override_env_once;
+
+void set_override(const Plan* p) {
+  std::lock_guard<std::mutex> lock(g_override_mu);
+  if (p) g_override_plan = *p;
+  g_override_set.store(p != nullptr, std::memory_order_release);
+}
+
+bool override_plan(Plan* out) {
+  std::call_once(g_override_env_once, [] {
+    const char* env = getenv("HP_RMS_NORM_PLAN");
+    Plan p;
+    if (env && *env && parse_plan(env, &p)) set_override(&p);
+  });
+  if (!g_override_set.load(std::memory_order_acquire)) return false;
+  std::lock_guard<std::mutex> lock(g_override_mu);
+  if (!g_override_set.load(std::memory_order_relaxed)) return false;
+  *out = g_override_plan;
+  return true;
+}
 
 bool parse_plan(const std::string& s, Plan* p) {
   char kind[16] = {0};
@@ -998,10 +1025,9 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   if (p.kind == kTwoPass && q.out_form != kOutSame)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "rows longer than 16384 vectors are supported with a "
                                            "16-bit output only");
-  if (g_override_set) {
-    Plan o;
+  Plan o;
+  if (override_plan(&o)) {
     std::string why;
-    if (!parse_plan(g_override, &o)) return fail(HPRN_ERR_INVALID_ARGUMENT, "unparsable plan override");
     if (o.vec > max_vec || q.hidden % (o.vec / 2) != 0)
       return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override vector width not allowed here");
     const int onvec = static_cast<int>(q.hidden / (o.vec / 2));
@@ -1170,15 +1196,15 @@ int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* inpu
 
 int hprn_set_plan_override(const char* plan) {
   using namespace hprn;
+  Plan unused;
+  override_plan(&unused);  // read the environment first, so this call wins over it
   if (!plan || !*plan) {
-    g_override_set = false;
-    g_override.clear();
+    set_override(nullptr);
     return ok();
   }
   Plan p;
   if (!parse_plan(plan, &p)) return fail(HPRN_ERR_INVALID_ARGUMENT, "unparsable plan override");
-  g_override = plan;
-  g_override_set = true;
+  set_override(&p);
   return ok();
 }
 

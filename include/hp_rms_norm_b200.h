@@ -205,11 +205,13 @@ HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const v
                                 int64_t residual_row_stride, char* plan, int plan_len);
 
 /*
- * Tuning hook: force the launch plan of every later hprn_rms_norm call in this
- * process (same string format as hprn_rms_norm_plan; NULL or "" restores the
- * built-in heuristic).  A forced plan that does not fit a call makes that call
- * fail with HPRN_ERR_INVALID_ARGUMENT.  Process-global, not thread-safe: meant
- * for benchmarks and launch-shape sweeps, not for production callers.
+ * Tuning hook: force the launch plan of every later hprn_rms_norm* call in
+ * this process (same string format as hprn_rms_norm_plan; NULL or "" restores
+ * the built-in heuristic).  The HP_RMS_NORM_PLAN environment variable, read at
+ * the first call, sets the same override.  A forced plan that does not fit a
+ * call makes that call fail with HPRN_ERR_INVALID_ARGUMENT.  Process-global
+ * (safe to call concurrently with launches): meant for benchmarks and
+ * launch-shape sweeps, not for production callers.
  */
 HPRN_API int hprn_set_plan_override(const char* plan);
 
