@@ -48,6 +48,7 @@ EXPORTED = (
     "hprn_version",
     "hprn_rms_norm_plan",
     "hprn_set_plan_override",
+    "hprn_wait_timeouts",
 )
 
 
@@ -98,6 +99,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_rms_norm_plan.restype = c_int
     lib.hprn_set_plan_override.argtypes = [ctypes.c_char_p]
     lib.hprn_set_plan_override.restype = c_int
+    lib.hprn_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint), c_int]
+    lib.hprn_wait_timeouts.restype = c_int
     _lib = lib
     return lib
 
@@ -174,6 +177,13 @@ def plan(rows: int, hidden: int, dtype: int = DTYPE_BF16, input_ptr: int = 0,
 
 def set_plan_override(plan_str: str | None) -> None:
     _check(load().hprn_set_plan_override(plan_str.encode() if plan_str else None))
+
+
+def wait_timeouts(reset: bool = False) -> int:
+    """CTAs on the current device that gave up a bounded wait (hprn_wait_timeouts)."""
+    n = ctypes.c_uint(0)
+    _check(load().hprn_wait_timeouts(ctypes.byref(n), 1 if reset else 0))
+    return int(n.value)
 
 
 def version() -> int:

@@ -33,7 +33,11 @@
 //     small enough for many to be resident per SM at every hidden size (no
 //     occupancy cliff at large hidden);
 //   * rows too long for the register-resident kernels use a two-pass kernel
-//     that re-reads its own just-written residual from L2, not HBM.
+//     that re-reads its own just-written residual from L2, not HBM;
+//   * a fifth kernel stages rows in shared memory with TMA bulk copies and
+//     mbarriers (plan kind "tma").  Timed against the register-resident
+//     kernels at every shape, it is never faster on the fused form, so the
+//     launch heuristic never picks it; forced plans reach it.
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -46,6 +50,7 @@
 #include <mutex>
 #include <string>
 
+#include "bulk.cuh"
 #include "runtime.cuh"
 #include "vec.cuh"
 
@@ -562,9 +567,144 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
 }
 
 // ---------------------------------------------------------------------------
+// Kernel 4: rows staged in shared memory by TMA bulk copies (16-bit output).
+// A persistent grid (as many CTAs as fit on the SMs) walks rows blockIdx.x,
+// + gridDim.x, ...; one thread issues, per row, a 1-D cp.async.bulk of the
+// input row (and one of the residual row) into a ring of `stages` row buffers,
+// each completing on its own mbarrier, so a CTA keeps `stages` rows in flight
+// with two instructions per row whatever the row length.  All threads wait on
+// the stage's mbarrier, take their 16- or 32-byte vectors from shared memory and
+// finish the row as the register kernels do.  The reduction barrier doubles as
+// the stage's release: right after it the issuing thread refills the stage
+// with the row `stages` ahead.  The weight stays in registers for every row.
+// A wait that gives up (a copy that never completed) ends the CTA after the
+// copies it still has in flight have landed, and counts in g_wait_timeouts.
+constexpr int kTmaMaxStages = 16;
+// Shared memory per CTA kept out of the dynamic ring: the mbarriers and the
+// reduction partials (384 bytes), rounded up.
+constexpr int kTmaStaticSmemReserve = 1024;
+
+__device__ unsigned int g_wait_timeouts;
+
+// Vector `v` (VEC bytes) of a row staged in shared memory, as 16-byte reads.
+template <int VEC>
+__device__ __forceinline__ Vec<VEC> ld_staged(const unsigned char* row, int v) {
+  Vec<VEC> out;
+  const uint4* p = reinterpret_cast<const uint4*>(row + static_cast<size_t>(v) * VEC);
+#pragma unroll
+  for (int k = 0; k < VEC / 16; ++k) {
+    const uint4 q = p[k];
+    out.w[4 * k] = q.x, out.w[4 * k + 1] = q.y, out.w[4 * k + 2] = q.z, out.w[4 * k + 3] = q.w;
+  }
+  return out;
+}
+
+template <typename T, int VEC, int VPT, bool RES>
+__global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_rows(RmsArgs a) {
+  static_assert(VEC == 16 || VEC == 32, "rows are staged as 16-byte pieces");
+  constexpr int EPV = Vec<VEC>::kElems;
+  extern __shared__ __align__(128) unsigned char stage_mem[];
+  __shared__ __align__(8) uint64_t full[kTmaMaxStages];
+  __shared__ float warp_part[2][32];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int nthreads = blockDim.x;
+  const int nwarps = nthreads >> 5;
+  const int stages = a.rows_per_cta;
+  const uint32_t row_bytes = static_cast<uint32_t>(a.nvec) * VEC;
+  const uint32_t stage_bytes = (RES ? 2u : 1u) * row_bytes;
+  const int64_t first = blockIdx.x;
+  const int64_t step = gridDim.x;
+  const int64_t count = first < a.rows ? (a.rows - 1 - first) / step + 1 : 0;
+  uint16_t* out = static_cast<uint16_t*>(a.out);
+  const uint64_t pol_stream = policy_evict_first();
+  const uint64_t pol_keep = policy_evict_last();
+
+  auto issue = [&](int64_t k, int s) {
+    const int64_t row = first + k * step;
+    const uint32_t bar = smem_u32(&full[s]);
+    const uint32_t dst = smem_u32(stage_mem + static_cast<size_t>(s) * stage_bytes);
+    mbar_arrive_expect_tx(bar, stage_bytes);
+    bulk_load(dst, a.x + row * a.x_stride, row_bytes, bar, pol_stream);
+    if constexpr (RES) bulk_load(dst + row_bytes, a.r + row * a.r_stride, row_bytes, bar, pol_stream);
+  };
+
+  pdl_entry();
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(smem_u32(&full[s]), 1);
+    mbar_init_fence();
+    for (int s = 0; s < stages && s < count; ++s) issue(s, s);
+  }
+  Vec<VEC> wv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = tid + j * nthreads;
+    if (v < a.nvec) wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
+  }
+  __syncthreads();
+
+  int s = 0;
+  uint32_t parity = 0;
+  for (int64_t k = 0; k < count; ++k) {
+    const int64_t row = first + k * step;
+    const bool arrived = mbar_wait_bounded(smem_u32(&full[s]), parity);
+    const unsigned char* xs = stage_mem + static_cast<size_t>(s) * stage_bytes;
+    uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
+    Vec<VEC> xv[VPT];
+    float a0 = 0.f, a1 = 0.f;
+    if (arrived) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = tid + j * nthreads;
+        if (v < a.nvec) {
+          xv[j] = ld_staged<VEC>(xs, v);
+          if constexpr (RES) {
+            add_round<T, VEC>(xv[j], ld_staged<VEC>(xs + row_bytes, v), a0, a1);
+            st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+          } else {
+            square_sum<T, VEC>(xv[j], a0, a1);
+          }
+        }
+      }
+    }
+    const float wsum = warp_sum(a0 + a1);
+    if (lane == 0) warp_part[k & 1][warp] = wsum;
+    // Every thread has read stage s (or some thread gave up waiting).
+    if (__syncthreads_or(!arrived)) {
+      if (tid == 0) {
+        // Let this CTA's copies still in flight land before its shared memory goes.
+        int ws = s;
+        uint32_t wp = parity;
+        for (int64_t j = k; j < count && j < k + stages; ++j) {
+          mbar_wait_bounded(smem_u32(&full[ws]), wp);
+          if (++ws == stages) ws = 0, wp ^= 1u;
+        }
+        atomicAdd(&g_wait_timeouts, 1u);
+      }
+      return;
+    }
+    if (tid == 0 && k + stages < count) {
+      fence_proxy_async_smem();
+      issue(k + stages, s);
+    }
+    const float total = warp_sum(lane < nwarps ? warp_part[k & 1][lane] : 0.f);
+    const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
+    uint16_t* orow = out + row * a.out_stride;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = tid + j * nthreads;
+      if (v < a.nvec)
+        st_global<VEC>(orow + static_cast<int64_t>(v) * EPV, normalize<T, VEC>(xv[j], wv[j], inv));
+    }
+    if (++s == stages) s = 0, parity ^= 1u;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Launch plans.
 
-enum Kind { kWarpRows = 0, kCtaRows = 1, kClusterRows = 2, kTwoPass = 3 };
+enum Kind { kWarpRows = 0, kCtaRows = 1, kClusterRows = 2, kTwoPass = 3, kTma = 4 };
 
 struct Plan {
   Kind kind = kWarpRows;
@@ -589,6 +729,7 @@ const char* kind_name(Kind k) {
     case kWarpRows: return "warp";
     case kCtaRows: return "cta";
     case kClusterRows: return "cluster";
+    case kTma: return "tma";
     default: return "twopass";
   }
 }
@@ -603,6 +744,8 @@ std::string plan_string(const Plan& p) {
 // VPT values compiled for each kind and variant (must match the dispatch
 // tables below).
 bool vpt_supported(Kind k, int vec, int vpt, const Variant& v) {
+  if (k == kTma)
+    return (vec == 16 || vec == 32) && v.out == kOutSame && (vpt == 1 || vpt == 2 || vpt == 4 || vpt == 8);
   if (!v.full()) {
     switch (k) {
       case kWarpRows: return vpt == 1 || vpt == 2 || vpt == 4;
@@ -740,6 +883,7 @@ bool parse_plan(const std::string& s, Plan* p) {
   else if (k == "cta") p->kind = kCtaRows;
   else if (k == "cluster") p->kind = kClusterRows;
   else if (k == "twopass") p->kind = kTwoPass;
+  else if (k == "tma") p->kind = kTma;
   else return false;
   p->vec = vec;
   p->vpt = vpt;
@@ -784,6 +928,15 @@ bool plan_valid(const Plan& p, int nvec, int max_vec, const Variant& var, std::s
       }
       return true;
     }
+    case kTma:
+      if (p.cluster != 1 || p.tpr < 32 || p.tpr > cta_max_threads(p.vpt * p.vec / 16) || p.tpr % 32 ||
+          static_cast<int64_t>(p.tpr) * p.vpt < nvec || p.rows_per_cta < 1 ||
+          p.rows_per_cta > kTmaMaxStages) {
+        *why = "tma plan needs cluster 1, tpr a multiple of 32 within the launch bound covering "
+               "the row, and 1..16 stages (rpc)";
+        return false;
+      }
+      return true;
     default:
       if (p.tpr < 32 || p.tpr > kTwoPassThreads || p.tpr % 32) {
         *why = "twopass tpr must be a multiple of 32 in [32, 512]";
@@ -832,9 +985,23 @@ KernelFn pick_cta(int vpt) {
   return nullptr;
 }
 
+template <typename T, int VEC, bool RES>
+KernelFn pick_tma(int vpt) {
+  switch (vpt) {
+    case 1: return rms_norm_tma_rows<T, VEC, 1, RES>;
+    case 2: return rms_norm_tma_rows<T, VEC, 2, RES>;
+    case 4: return rms_norm_tma_rows<T, VEC, 4, RES>;
+    case 8: return rms_norm_tma_rows<T, VEC, 8, RES>;
+  }
+  return nullptr;
+}
+
 template <typename T, int VEC, bool RES, int OUT>
 KernelFn pick_kind(const Plan& p) {
   switch (p.kind) {
+    case kTma:
+      if constexpr ((VEC == 16 || VEC == 32) && OUT == kOutSame) return pick_tma<T, VEC, RES>(p.vpt);
+      return nullptr;
     case kWarpRows: return pick_warp<T, VEC, RES, OUT>(p.vpt);
     case kCtaRows: return pick_cta<T, VEC, false, RES, OUT>(p.vpt);
     case kClusterRows: return pick_cta<T, VEC, true, RES, OUT>(p.vpt);
@@ -1058,10 +1225,71 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   return HPRN_OK;
 }
 
-int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, cudaStream_t stream,
-           unsigned flags) {
+// Resident CTAs per SM of a TMA-staged kernel at `threads` threads and `smem`
+// bytes of ring, cached per (device, kernel, threads, smem); 0 on error.
+int tma_ctas_per_sm(const DeviceInfo* dev, KernelFn fn, int threads, int smem) {
+  struct Entry {
+    int device;
+    KernelFn fn;
+    int threads, smem, ctas;
+  };
+  static std::mutex mu;
+  static Entry cache[128];
+  static int used = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].device == dev->device && cache[i].fn == fn && cache[i].threads == threads &&
+        cache[i].smem == smem)
+      return cache[i].ctas;
+  const int max_dyn = static_cast<int>(dev->smem_per_block_optin) - kTmaStaticSmemReserve;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
+    return 0;
+  int ctas = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, fn, threads, smem) != cudaSuccess) return 0;
+  if (used < 128) cache[used++] = Entry{dev->device, fn, threads, smem, ctas};
+  return ctas;
+}
+
+// One persistent launch of the TMA-staged kernel: as many CTAs as are
+// resident at once (or one per row when there are fewer rows).
+int launch_tma(const Plan& p, const RmsArgs& a, KernelFn fn, const DeviceInfo* dev,
+               cudaStream_t stream, unsigned flags) {
+  const int64_t stage_bytes = static_cast<int64_t>(a.r ? 2 : 1) * a.nvec * p.vec;
+  const int64_t smem = stage_bytes * p.rows_per_cta;
+  if (smem > static_cast<int64_t>(dev->smem_per_block_optin) - kTmaStaticSmemReserve)
+    return fail(HPRN_ERR_INVALID_ARGUMENT,
+                "tma plan " + plan_string(p) + " needs more shared memory than one CTA has");
+  const int per_sm = tma_ctas_per_sm(dev, fn, p.tpr, static_cast<int>(smem));
+  if (per_sm < 1) {
+    cudaGetLastError();
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "tma plan " + plan_string(p) + " fits no SM");
+  }
+  const int64_t resident = static_cast<int64_t>(per_sm) * dev->sm_count;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(static_cast<unsigned>(a.rows < resident ? a.rows : resident), 1, 1);
+  cfg.blockDim = dim3(p.tpr, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 0;
+  if (flags & HPRN_LAUNCH_PDL) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+  if (e != cudaSuccess)
+    return fail(HPRN_ERR_CUDA, std::string("rms_norm launch failed (") + plan_string(p) +
+                                   "): " + cudaGetErrorString(e));
+  return HPRN_OK;
+}
+
+int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const DeviceInfo* dev,
+           cudaStream_t stream, unsigned flags) {
   KernelFn fn = pick_kernel(dtype, p, var);
   if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
+  if (p.kind == kTma) return launch_tma(p, a, fn, dev, stream, flags);
   // Rows handled per CTA-group in grid.x; split very tall problems into launches.
   const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;
   const int64_t ctas_per_unit = p.kind == kClusterRows ? p.cluster : 1;
@@ -1122,7 +1350,7 @@ int run(const Problem& q, void* stream, unsigned flags) {
   Plan p;
   RmsArgs a;
   if ((st = make_plan(q, var, &p, &a)) != HPRN_OK) return st;
-  if ((st = launch(p, a, q.dtype, var, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK)
+  if ((st = launch(p, a, q.dtype, var, dev, static_cast<cudaStream_t>(stream), flags)) != HPRN_OK)
     return st;
   return ok();
 }
@@ -1191,6 +1419,24 @@ int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* inpu
   const int st = make_plan(q, Variant{true, kOutSame}, &p, &a);
   if (st != HPRN_OK) return st;
   snprintf(plan, plan_len, "%s", plan_string(p).c_str());
+  return ok();
+}
+
+int hprn_wait_timeouts(unsigned int* count, int reset) {
+  using namespace hprn;
+  if (!count) return fail(HPRN_ERR_INVALID_ARGUMENT, "count pointer required");
+  const DeviceInfo* dev = nullptr;
+  int st = current_device(&dev);
+  if (st != HPRN_OK) return st;
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_wait_timeouts, sizeof(v));
+  if (e == cudaSuccess && reset && v) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_wait_timeouts, &zero, sizeof(zero));
+  }
+  if (e != cudaSuccess)
+    return fail(HPRN_ERR_CUDA, std::string("reading the wait-timeout count: ") + cudaGetErrorString(e));
+  *count = v;
   return ok();
 }
 

@@ -2,6 +2,7 @@
 
     python -m hp_rms_norm_b200.tune [--rows 4096] [--hidden 1024,2048,...]
                                     [--dtype bf16|fp16] [--warm] [--json out.json]
+                                    [--no-tma | --tma-only] [--isolated]
                                     [--variant fused|fused_out|plain|fused_fp8s|fused_fp8d|
                                                plain_fp8s|plain_fp8d]
 
@@ -9,7 +10,9 @@ Times every compiled launch plan that covers each requested shape (through
 ``hprn_set_plan_override``) and prints the fastest, next to the built-in
 heuristic's choice.  Timing: a CUDA graph of back-to-back launches over
 rotating buffer sets of at least 600 MB, so every launch reads cold data (or
-one buffer set with ``--warm``), replayed three times after one warm replay.
+one buffer set with ``--warm``), replayed three times after one warm replay;
+with ``--isolated``, the median of single launches each preceded by an L2
+flush.
 
 This is how the heuristic in csrc/rms_norm.cu (``default_plan``) was fitted on
 B200; rerun it to check the heuristic on another part or other shapes.
@@ -35,6 +38,31 @@ VARIANTS = {
     "fused_nvfp4": (True, "nvfp4", 6.5625),
     "plain_nvfp4": (False, "nvfp4", 2.5625),
 }
+
+
+# Shared memory one CTA may use for a TMA ring on B200 (227 KB, less the
+# kernel's mbarriers and partials).
+TMA_SMEM = 232448 - 1024
+
+
+def tma_candidates(hidden: int, residual: bool) -> list[str]:
+    """TMA-staged plans (16- or 32-byte vectors, persistent grid) covering
+    `hidden`, for ring depths whose buffers fit one CTA."""
+    stage = (2 if residual else 1) * hidden * 2
+    out = []
+    for vec in (16, 32):
+        if hidden % (vec // 2):
+            continue
+        nv = hidden // (vec // 2)
+        for vpt in (1, 2, 4, 8):
+            load = vpt * vec // 16  # 16-byte pieces per thread
+            max_threads = 1024 if load <= 2 else (512 if load <= 4 else 256)
+            tpr = -(-(-(-nv // vpt)) // 32) * 32
+            if tpr > max_threads or (tpr > 32 and (tpr - 32) * vpt >= nv):
+                continue
+            out += [f"tma:vec{vec}:vpt{vpt}:tpr{tpr}:cluster1:rpc{st}"
+                    for st in (1, 2, 3, 4, 6, 8) if st * stage <= TMA_SMEM]
+    return out
 
 
 def candidates(nvec: int, full: bool = True) -> list[str]:
@@ -82,8 +110,26 @@ def graph_us(torch, fn, nsets: int, reps: int = 3) -> float:
     return e0.elapsed_time(e1) * 1e3 / (reps * L)
 
 
+def isolated_us(torch, fn, nsets: int, flush, reps: int = 7) -> float:
+    """Median time of one launch on its own: L2 flushed (a write of a buffer
+    larger than L2), then the launch alone between two events."""
+    s = torch.cuda.current_stream()
+    ts = []
+    for k in range(reps + 1):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn(k % nsets, s.cuda_stream)
+        e1.record()
+        torch.cuda.synchronize()
+        if k:
+            ts.append(e0.elapsed_time(e1) * 1e3)
+    return sorted(ts)[len(ts) // 2]
+
+
 def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False,
-          variant: str = "fused") -> dict:
+          variant: str = "fused", tma: bool = True, tma_only: bool = False,
+          isolated: bool = False) -> dict:
     import torch
 
     from . import capi
@@ -95,6 +141,9 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     code = capi.DTYPE_BF16 if dtype == "bf16" else capi.DTYPE_FP16
     dev = torch.device("cuda", torch.cuda.current_device())
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if isolated else None
+    time_us = (lambda fn, n: isolated_us(torch, fn, n, flush)) if isolated else \
+        (lambda fn, n: graph_us(torch, fn, n))
     results = {}
     for h in hiddens:
         set_bytes = rows * h * 2 * 2
@@ -127,17 +176,20 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
 
         timings = {}
         try:
-            for p in candidates(h // 16, variant == "fused") if h % 16 == 0 else []:
+            plans = candidates(h // 16, variant == "fused") if h % 16 == 0 else []
+            if form == capi.OUT_SAME and (tma or tma_only) and h % 8 == 0:
+                plans = (plans if not tma_only else []) + tma_candidates(h, res_needed)
+            for p in plans:
                 capi.set_plan_override(p)
                 try:
-                    timings[p] = round(graph_us(torch, run, nsets), 2)
+                    timings[p] = round(time_us(run, nsets), 2)
                 except capi.HprnError:
                     pass  # plan not compiled for this variant (e.g. over its launch bound)
         finally:
             capi.set_plan_override(None)
         default = capi.plan(rows, h, code, xs[0].data_ptr(), rs[0].data_ptr()) \
             if variant == "fused" else "default"
-        t_default = round(graph_us(torch, run, nsets), 2)
+        t_default = round(time_us(run, nsets), 2)
         best = min(timings, key=timings.get) if timings else default
         results[h] = {"default": default, "default_us": t_default,
                       "default_gbs": round(byt / t_default / 1e3, 1),
@@ -156,8 +208,13 @@ def main() -> None:
     ap.add_argument("--warm", action="store_true")
     ap.add_argument("--json", default=None)
     ap.add_argument("--variant", choices=list(VARIANTS), default="fused")
+    ap.add_argument("--no-tma", action="store_true", help="leave out the TMA-staged plans")
+    ap.add_argument("--tma-only", action="store_true", help="time only the TMA-staged plans")
+    ap.add_argument("--isolated", action="store_true",
+                    help="time single launches after an L2 flush instead of back-to-back graphs")
     a = ap.parse_args()
-    res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm, a.variant)
+    res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm, a.variant,
+                tma=not a.no_tma, tma_only=a.tma_only, isolated=a.isolated)
     print(f"{'hidden':>7} {'default plan':40} {'us':>8} {'GB/s':>8}   {'best plan':40} {'us':>8}")
     for h, r in res.items():
         print(f"{h:>7} {r['default']:40} {r['default_us']:>8} {r['default_gbs']:>8}   "

@@ -195,9 +195,9 @@ HPRN_API int hprn_version(void);
  * Launch-plan introspection (for tests and benchmarks): writes the plan that
  * hprn_rms_norm would use for this problem on the current device into
  * `plan` as a NUL-terminated string "<kind>:vec<V>:vpt<P>:tpr<T>:cluster<C>:rpc<R>"
- * (kind warp | cta | cluster | twopass; V bytes per vector access; P vectors
- * per thread; T threads per CTA; C CTAs per row; R rows per CTA) and returns
- * HPRN_OK.  Performs no launch.  Null input/residual pointers plan for
+ * (kind warp | cta | cluster | twopass | tma; V bytes per vector access; P
+ * vectors per thread; T threads per CTA; C CTAs per row; R rows per CTA, or for
+ * kind tma the depth of the CTA's ring of TMA-staged rows) and returns HPRN_OK.  Performs no launch.  Null input/residual pointers plan for
  * 256-byte-aligned tensors; without a usable device it plans for a 148-SM B200.
  */
 HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* input,
@@ -214,6 +214,17 @@ HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const v
  * launch-shape sweeps, not for production callers.
  */
 HPRN_API int hprn_set_plan_override(const char* plan);
+
+/*
+ * No reference counterpart.  Kernels that stage rows through TMA bulk copies
+ * wait on mbarriers with a bound (one second); a CTA that gives up a wait
+ * leaves its remaining rows unwritten and counts itself here, on its device.
+ * Writes the current device's count into *count and, if `reset` is non-zero,
+ * clears it.  Synchronous; synchronise the streams that launched the kernels
+ * first.  A non-zero count means the launches since the last reset produced
+ * incomplete results.
+ */
+HPRN_API int hprn_wait_timeouts(unsigned int* count, int reset);
 
 #ifdef __cplusplus
 }

@@ -131,5 +131,11 @@ def test_relu_argument_errors_before_any_launch():
 def test_plan_override_parsing():
     expect_error(lambda: capi.set_plan_override("nonsense"), capi.ERR_INVALID_ARGUMENT, "unparsable")
     capi.set_plan_override("cta:vec32:vpt2:tpr128:cluster1:rpc1")
+    capi.set_plan_override("tma:vec16:vpt1:tpr128:cluster1:rpc4")
     capi.set_plan_override(None)
     assert capi.plan(4096, 4096).startswith("cta:")
+
+
+def test_wait_timeouts_needs_a_count_pointer():
+    lib = capi.load()
+    assert lib.hprn_wait_timeouts(None, 0) == capi.ERR_INVALID_ARGUMENT
