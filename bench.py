@@ -206,6 +206,11 @@ class ClockSampler:
 # --------------------------------------------------------------------------
 # Measurement helpers.
 
+# Nominal B200 HBM3e bandwidth (~8 TB/s); fractions of it are reported next to
+# the fraction of the measured copy bandwidth, which is the roofline denominator.
+NOMINAL_HBM_GBS = 8000.0
+
+
 def measured_peak():
     """Measured HBM copy bandwidth of this pool (driver-written), else fallback."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -464,6 +469,7 @@ def run_ours(args, dist):
                        "bytes_per_step": step_bytes, "parallelism": f"rows sharded x{dist.world}, "
                        "no collective"},
             "frac_of_peak": round(value / dist.world / peak, 3),
+            "frac_of_nominal_peak": round(value / dist.world / NOMINAL_HBM_GBS, 3),
             "gpu_launches": K * len(shapes),
             "gpu_launches_note": "one hprn_rms_norm kernel launch per shape per timed step",
             "roofline": roofline, "per_shape": per_shape,
