@@ -86,8 +86,15 @@ struct RmsArgs {
   float inv_hidden;
 };
 
+// Element pairs go through Blackwell's packed fp32 instructions
+// (__fadd2_rn / __fmul2_rn / __ffma2_rn: add/mul/fma.rn.f32x2).  Each lane
+// rounds exactly as the scalar fp32 instruction does (nearest even, no flush
+// to zero), so the results are those of scalar code, bit for bit, at half the
+// arithmetic instructions.
+
 // Adds residual into input in fp32, keeps the rounded sum in `xv`, and
-// accumulates the squares of the unrounded sums.
+// accumulates the squares of the unrounded sums (even elements into a0, odd
+// into a1).
 template <typename T, int VEC>
 __device__ __forceinline__ void add_round(Vec<VEC>& xv, const Vec<VEC>& rv, float& a0, float& a1) {
   if constexpr (VEC == 2) {
@@ -95,16 +102,15 @@ __device__ __forceinline__ void add_round(Vec<VEC>& xv, const Vec<VEC>& rv, floa
     a0 = fmaf(s, s, a0);
     xv.h = pack1<T>(s);
   } else {
+    float2 acc = make_float2(a0, a1);
 #pragma unroll
     for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-      const float2 a = unpack2<T>(xv.w[k]);
-      const float2 b = unpack2<T>(rv.w[k]);
-      const float s0 = a.x + b.x;
-      const float s1 = a.y + b.y;
-      a0 = fmaf(s0, s0, a0);
-      a1 = fmaf(s1, s1, a1);
-      xv.w[k] = pack2<T>(s0, s1);
+      const float2 s = __fadd2_rn(unpack2<T>(xv.w[k]), unpack2<T>(rv.w[k]));
+      acc = __ffma2_rn(s, s, acc);
+      xv.w[k] = pack2<T>(s.x, s.y);
     }
+    a0 = acc.x;
+    a1 = acc.y;
   }
 }
 
@@ -115,12 +121,14 @@ __device__ __forceinline__ void square_sum(const Vec<VEC>& xv, float& a0, float&
     const float s = unpack1<T>(xv.h);
     a0 = fmaf(s, s, a0);
   } else {
+    float2 acc = make_float2(a0, a1);
 #pragma unroll
     for (int k = 0; k < Vec<VEC>::kWords; ++k) {
       const float2 a = unpack2<T>(xv.w[k]);
-      a0 = fmaf(a.x, a.x, a0);
-      a1 = fmaf(a.y, a.y, a1);
+      acc = __ffma2_rn(a, a, acc);
     }
+    a0 = acc.x;
+    a1 = acc.y;
   }
 }
 
@@ -131,26 +139,27 @@ __device__ __forceinline__ Vec<VEC> normalize(const Vec<VEC>& rv, const Vec<VEC>
   if constexpr (VEC == 2) {
     o.h = pack1<T>(unpack1<T>(rv.h) * unpack1<T>(wv.h) * inv);
   } else {
+    const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
     for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-      const float2 a = unpack2<T>(rv.w[k]);
-      const float2 b = unpack2<T>(wv.w[k]);
-      o.w[k] = pack2<T>(a.x * b.x * inv, a.y * b.y * inv);
+      const float2 y = __fmul2_rn(__fmul2_rn(unpack2<T>(rv.w[k]), unpack2<T>(wv.w[k])), inv2);
+      o.w[k] = pack2<T>(y.x, y.y);
     }
   }
   return o;
 }
 
-// max_j |y_j| over one vector, folded into m (NaNs are ignored, as by fmaxf).
+// max_j |f32(r_j) * f32(w_j)| over one vector, folded into m (NaNs are
+// ignored, as by fmaxf).  The row's amax of y_j = (r_j * w_j) * inv is this
+// times inv, rounded once: inv > 0 and round-to-nearest is monotone, so
+// max_j |RN(p_j * inv)| = RN(max_j |p_j| * inv) exactly, with one multiply
+// per row instead of one per element.
 template <typename T, int VEC>
-__device__ __forceinline__ float vec_amax(const Vec<VEC>& rv, const Vec<VEC>& wv, float inv,
-                                          float m) {
+__device__ __forceinline__ float vec_amax_rw(const Vec<VEC>& rv, const Vec<VEC>& wv, float m) {
 #pragma unroll
   for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-    const float2 a = unpack2<T>(rv.w[k]);
-    const float2 b = unpack2<T>(wv.w[k]);
-    m = fmaxf(m, fabsf(a.x * b.x * inv));
-    m = fmaxf(m, fabsf(a.y * b.y * inv));
+    const float2 p = __fmul2_rn(unpack2<T>(rv.w[k]), unpack2<T>(wv.w[k]));
+    m = fmaxf(m, fmaxf(fabsf(p.x), fabsf(p.y)));
   }
   return m;
 }
@@ -163,13 +172,14 @@ __device__ __forceinline__ Vec<VEC / 2> quantize_e4m3(const Vec<VEC>& rv, const 
   static_assert(VEC >= 8, "fp8 output needs at least 4 elements per vector");
   Vec<VEC / 2> o;
 #pragma unroll
+  const float2 inv2 = make_float2(inv, inv);
+  const float2 is2 = make_float2(inv_scale, inv_scale);
   for (int k = 0; k < Vec<VEC>::kWords; k += 2) {
     uint32_t word = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float2 a = unpack2<T>(rv.w[k + h]);
-      const float2 b = unpack2<T>(wv.w[k + h]);
-      const float2 q = make_float2(a.x * b.x * inv * inv_scale, a.y * b.y * inv * inv_scale);
+      const float2 y = __fmul2_rn(__fmul2_rn(unpack2<T>(rv.w[k + h]), unpack2<T>(wv.w[k + h])), inv2);
+      const float2 q = __fmul2_rn(y, is2);
       const __nv_fp8x2_storage_t p = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
       word |= static_cast<uint32_t>(p) << (16 * h);
     }
@@ -185,29 +195,26 @@ __device__ __forceinline__ Vec<VEC / 2> quantize_e4m3(const Vec<VEC>& rv, const 
 template <typename T>
 __device__ __forceinline__ Vec<8> quantize_nvfp4(const Vec<32>& rv, const Vec<32>& wv, float inv,
                                                  float gs, uint8_t* sf_out) {
-  float y[16];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float2 a = unpack2<T>(rv.w[k]);
-    const float2 b = unpack2<T>(wv.w[k]);
-    y[2 * k] = a.x * b.x * inv;
-    y[2 * k + 1] = a.y * b.y * inv;
-  }
+  float2 y[8];
+  const float2 inv2 = make_float2(inv, inv);
   float amax = 0.f;
 #pragma unroll
-  for (int k = 0; k < 16; ++k) amax = fmaxf(amax, fabsf(y[k]));
+  for (int k = 0; k < 8; ++k) {
+    y[k] = __fmul2_rn(__fmul2_rn(unpack2<T>(rv.w[k]), unpack2<T>(wv.w[k])), inv2);
+    amax = fmaxf(amax, fmaxf(fabsf(y[k].x), fabsf(y[k].y)));
+  }
   const __nv_fp8_storage_t sf = __nv_cvt_float_to_fp8(gs * (amax / 6.0f), __NV_SATFINITE, __NV_E4M3);
   const float sfv = __half2float(__half(__nv_cvt_fp8_to_halfraw(sf, __NV_E4M3)));
   const float qs = sfv != 0.f ? gs / sfv : 0.f;
+  const float2 qs2 = make_float2(qs, qs);
   Vec<8> o;
 #pragma unroll
   for (int w = 0; w < 2; ++w) {
     uint32_t word = 0;
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
-      const int k = 8 * w + 2 * b;
       const __nv_fp4x2_storage_t p =
-          __nv_cvt_float2_to_fp4x2(make_float2(y[k] * qs, y[k + 1] * qs), __NV_E2M1, cudaRoundNearest);
+          __nv_cvt_float2_to_fp4x2(__fmul2_rn(y[4 * w + b], qs2), __NV_E2M1, cudaRoundNearest);
       word |= static_cast<uint32_t>(p) << (8 * b);
     }
     o.w[w] = word;
@@ -351,16 +358,20 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
       if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
     }
   }
-  const float inv = rsqrtf(fmaf(warp_sum(a0 + a1), a.inv_hidden, a.eps));
-  float inv_scale = static_inv_scale<OUT>(a);
+  // Dynamic fp8: max |r * w| does not depend on inv, so it is reduced next to
+  // the sum of squares and scaled by inv once (see vec_amax_rw).
+  float m = 0.f;
   if constexpr (OUT == kOutFp8Dynamic) {
-    float m = 0.f;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = lane + 32 * j;
-      if (v < a.nvec) m = vec_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv, m);
+      if (v < a.nvec) m = vec_amax_rw<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), m);
     }
-    const float scale = fmaxf(warp_max(m), kMinAmax) / kE4m3Max;
+  }
+  const float inv = rsqrtf(fmaf(warp_sum(a0 + a1), a.inv_hidden, a.eps));
+  float inv_scale = static_inv_scale<OUT>(a);
+  if constexpr (OUT == kOutFp8Dynamic) {
+    const float scale = fmaxf(warp_max(m) * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
     if (lane == 0) a.row_scales[row] = scale;
   }
@@ -445,38 +456,43 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
     }
   }
 
+  // Dynamic fp8: max |r * w| does not depend on inv, so it travels with the
+  // sum of squares through the same barrier (and cluster phase) and is scaled
+  // by inv once at the end (see vec_amax_rw).
+  constexpr bool kAmax = OUT == kOutFp8Dynamic;
+  float m = 0.f;
+  if constexpr (kAmax) {
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = v_begin + tid + j * nthreads;
+      if (v < v_end) m = vec_amax_rw<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), m);
+    }
+  }
   const float wsum = warp_sum(a0 + a1);
-  if (lane == 0) warp_part[warp] = wsum;
+  if constexpr (kAmax) m = warp_max(m);
+  if (lane == 0) {
+    warp_part[warp] = wsum;
+    if constexpr (kAmax) warp_amax[warp] = m;
+  }
   __syncthreads();
   float total = warp_sum(lane < nwarps ? warp_part[lane] : 0.f);
+  float amax = kAmax ? warp_max(lane < nwarps ? warp_amax[lane] : 0.f) : 0.f;
   if constexpr (CLUSTER) {
     cluster_wait();  // phase 1: all peers are running
-    if (warp == 0 && lane < static_cast<int>(csize)) st_cluster_f32(&cta_part[crank], lane, total);
+    if (warp == 0 && lane < static_cast<int>(csize)) {
+      st_cluster_f32(&cta_part[crank], lane, total);
+      if constexpr (kAmax) st_cluster_f32(&cta_amax[crank], lane, amax);
+    }
     cluster_arrive_release();
-    cluster_wait();  // phase 2: every CTA's partial has landed in every CTA
+    cluster_wait();  // phase 2: every CTA's partials have landed in every CTA
     total = warp_sum(lane < static_cast<int>(csize) ? cta_part[lane] : 0.f);
+    if constexpr (kAmax) amax = warp_max(lane < static_cast<int>(csize) ? cta_amax[lane] : 0.f);
   }
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
 
   float inv_scale = static_inv_scale<OUT>(a);
-  if constexpr (OUT == kOutFp8Dynamic) {
-    float m = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int v = v_begin + tid + j * nthreads;
-      if (v < v_end) m = vec_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv, m);
-    }
-    m = warp_max(m);
-    if (lane == 0) warp_amax[warp] = m;
-    __syncthreads();
-    float amax = warp_max(lane < nwarps ? warp_amax[lane] : 0.f);
-    if constexpr (CLUSTER) {
-      if (warp == 0 && lane < static_cast<int>(csize)) st_cluster_f32(&cta_amax[crank], lane, amax);
-      cluster_arrive_release();
-      cluster_wait();  // phase 3: every CTA's amax has landed in every CTA
-      amax = warp_max(lane < static_cast<int>(csize) ? cta_amax[lane] : 0.f);
-    }
-    const float scale = fmaxf(amax, kMinAmax) / kE4m3Max;
+  if constexpr (kAmax) {
+    const float scale = fmaxf(amax * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
     if (crank == 0 && tid == 0) a.row_scales[row] = scale;
   }
@@ -783,13 +799,13 @@ int round_up(int v, int m) { return (v + m - 1) / m * m; }
 // vectors per thread in smaller CTAs as rows grow.  Vectors per thread for a
 // one-CTA row of nvec vectors, or 0 for the warp-per-row kernel:
 int extended_vpt(int nvec, bool residual, int out) {
-  if (residual) return out == kOutNvfp4 ? (nvec <= 256 ? 1 : 2) : -1;  // -1: the fused rule
+  if (residual) return out == kOutNvfp4 ? (nvec <= 768 ? 1 : 2) : -1;  // -1: the fused rule
   if (nvec <= 64) return 0;
   switch (out) {
     case kOutSame: return nvec <= 128 ? 0 : (nvec <= 256 ? 1 : 2);
     case kOutFp8Static: return nvec <= 128 ? 0 : (nvec <= 1024 ? 2 : 4);
     case kOutFp8Dynamic: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
-    default: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : (nvec <= 1536 ? 4 : 2));  // NVFP4
+    default: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);  // NVFP4 (past 1536: a cluster)
   }
 }
 
@@ -803,7 +819,18 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
     p.kind = kWarpRows;
     p.vpt = nvec <= 64 ? (nvec + 31) / 32 : 4;
     p.tpr = 32;
-    p.rows_per_cta = residual ? 2 : 4;
+    // Quantised outputs: eight warp-rows per CTA (the re-tuned sweep's best at
+    // hidden 1024-2048, 1-7% over two or four).
+    p.rows_per_cta = out != kOutSame ? 8 : (residual ? 2 : 4);
+    return p;
+  }
+  if (!residual && out == kOutNvfp4 && nvec > 1536 && nvec <= 2048) {
+    // Plain NVFP4 rows of 1537..2048 vectors: a 4-CTA cluster at four vectors
+    // per thread beat every one-CTA plan (88 vs 94 us at 4096 x 32768).
+    p.kind = kClusterRows;
+    p.cluster = 4;
+    p.vpt = 4;
+    p.tpr = round_up(((nvec + 3) / 4 + 3) / 4, 32);
     return p;
   }
   if (ext > 0) {
