@@ -788,7 +788,7 @@ int round_up(int v, int m) { return (v + m - 1) / m * m; }
 //   * one CTA per row with as many threads as the row has 32-byte vectors
 //     (one vector per thread): the most warps per SM, so the most loads in
 //     flight, and the shortest serial chain per thread;
-//   * rows of at most 64 vectors: one warp per row, two rows per CTA;
+//   * rows of at most 64 vectors: one warp per row, eight rows per CTA;
 //   * rows of 1025..2048 vectors: two vectors per thread (four below ~1440
 //     vectors, where 1024-thread CTAs would leave SMs a CTA short);
 //   * thread-block clusters only once a row no longer fits one CTA: splitting
@@ -819,9 +819,10 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
     p.kind = kWarpRows;
     p.vpt = nvec <= 64 ? (nvec + 31) / 32 : 4;
     p.tpr = 32;
-    // Quantised outputs: eight warp-rows per CTA (the re-tuned sweep's best at
-    // hidden 1024-2048, 1-7% over two or four).
-    p.rows_per_cta = out != kOutSame ? 8 : (residual ? 2 : 4);
+    // Eight warp-rows (256 threads) per CTA: best or level for every form at
+    // hidden 1024-2048 (fused 6.60 vs 7.13 us with two at 4096 x 1024; plain
+    // 7.03 vs 7.57 us with four at 4096 x 2048).
+    p.rows_per_cta = 8;
     return p;
   }
   if (!residual && out == kOutNvfp4 && nvec > 1536 && nvec <= 2048) {

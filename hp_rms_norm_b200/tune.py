@@ -2,7 +2,7 @@
 
     python -m hp_rms_norm_b200.tune [--rows 4096] [--hidden 1024,2048,...]
                                     [--dtype bf16|fp16] [--warm] [--json out.json]
-                                    [--no-tma | --tma-only] [--isolated]
+                                    [--no-tma | --tma-only] [--isolated] [--copy]
                                     [--variant fused|fused_out|plain|fused_fp8s|fused_fp8d|
                                                plain_fp8s|plain_fp8d]
 
@@ -129,7 +129,7 @@ def isolated_us(torch, fn, nsets: int, flush, reps: int = 7) -> float:
 
 def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False,
           variant: str = "fused", tma: bool = True, tma_only: bool = False,
-          isolated: bool = False) -> dict:
+          isolated: bool = False, copy: bool = False) -> dict:
     import torch
 
     from . import capi
@@ -195,6 +195,18 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
                       "default_gbs": round(byt / t_default / 1e3, 1),
                       "best": best, "best_us": timings.get(best, t_default),
                       "plans": timings, "buffer_sets": nsets, "bytes_per_launch": byt}
+        if copy:
+            # torch's copy_ moving the same bytes (the kernel's reads into as
+            # many bytes of writes), timed the same way.  The size is rounded
+            # down to whole 4 KB: device-to-device copies of other sizes ran at
+            # under half the bandwidth on B200.
+            elems = byt // 4 // 2048 * 2048
+            srcs = [torch.empty(elems, device=dev, dtype=tdt) for _ in range(nsets)]
+            dsts = [torch.empty(elems, device=dev, dtype=tdt) for _ in range(nsets)]
+            t_copy = round(time_us(lambda k, s: dsts[k].copy_(srcs[k]), nsets), 2)
+            results[h]["copy_us"] = t_copy
+            results[h]["copy_gbs"] = round(4 * elems / t_copy / 1e3, 1)
+            del srcs, dsts
         del xs, rs, outs
         torch.cuda.empty_cache()
     return results
@@ -212,13 +224,17 @@ def main() -> None:
     ap.add_argument("--tma-only", action="store_true", help="time only the TMA-staged plans")
     ap.add_argument("--isolated", action="store_true",
                     help="time single launches after an L2 flush instead of back-to-back graphs")
+    ap.add_argument("--copy", action="store_true",
+                    help="also time torch's copy_ of the same bytes, the same way")
     a = ap.parse_args()
     res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm, a.variant,
-                tma=not a.no_tma, tma_only=a.tma_only, isolated=a.isolated)
-    print(f"{'hidden':>7} {'default plan':40} {'us':>8} {'GB/s':>8}   {'best plan':40} {'us':>8}")
+                tma=not a.no_tma, tma_only=a.tma_only, isolated=a.isolated, copy=a.copy)
+    print(f"{'hidden':>7} {'default plan':40} {'us':>8} {'GB/s':>8}   {'best plan':40} {'us':>8}"
+          + (f" {'copy us':>8} {'copy GB/s':>9}" if a.copy else ""))
     for h, r in res.items():
         print(f"{h:>7} {r['default']:40} {r['default_us']:>8} {r['default_gbs']:>8}   "
-              f"{r['best']:40} {r['best_us']:>8}")
+              f"{r['best']:40} {r['best_us']:>8}"
+              + (f" {r['copy_us']:>8} {r['copy_gbs']:>9}" if a.copy else ""))
     if a.json:
         with open(a.json, "w") as f:
             json.dump(res, f, indent=1)

@@ -56,7 +56,7 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     assert capi.plan(4096, 16384) == capi.plan(4096, 16384, input_ptr=1 << 20,
                                                residual_ptr=1 << 21)
     assert capi.plan(4096, 16384) == "cta:vec32:vpt1:tpr1024:cluster1:rpc1"
-    assert capi.plan(4096, 1024) == "warp:vec32:vpt2:tpr32:cluster1:rpc2"
+    assert capi.plan(4096, 1024) == "warp:vec32:vpt2:tpr32:cluster1:rpc8"
 
 
 def test_plan_vector_width_follows_alignment_and_hidden():
