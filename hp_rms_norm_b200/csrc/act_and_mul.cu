@@ -9,7 +9,11 @@
 //   gelu(a)      = a / 2 * (1 + erf(a / sqrt(2)))
 //   gelu_tanh(a) = a / 2 * (1 + tanh(sqrt(2 / pi) * (a + 0.044715 a^3)))
 // (Hendrycks & Gimpel, "Gaussian Error Linear Units", 2016), evaluated in fp32
-// with CUDA's expf / erff / tanhf, times f32(up), rounded once to T.
+// with CUDA's expf / erff / tanhf, times f32(up), rounded once to T.  SiLU's
+// division is __fdividef (reciprocal approximation and one multiply, within 2
+// fp32 ulp): the IEEE division costs more issue slots than the element's 6
+// bytes take on the memory side, and 2 fp32 ulp is far below half an ulp of
+// the 16-bit result.
 //
 // Bandwidth-bound: 6 bytes per output element (gate and up read, out
 // written).  Each thread keeps U vectors of gate and of up in flight (32-byte
@@ -28,7 +32,8 @@ namespace hprn {
 template <int ACT>
 __device__ __forceinline__ float activate(float a) {
   if constexpr (ACT == HPRN_ACT_SILU) {
-    return a / (1.0f + expf(-a));
+    // -a past ~88.7 makes the denominator +inf and the result -0 (a * 0).
+    return __fdividef(a, 1.0f + expf(-a));
   } else if constexpr (ACT == HPRN_ACT_GELU) {
     return 0.5f * a * (1.0f + erff(a * 0.70710678118654752f));
   } else {
@@ -46,8 +51,9 @@ __device__ __forceinline__ Vec<VEC> act_mul(const Vec<VEC>& g, const Vec<VEC>& u
 #pragma unroll
     for (int k = 0; k < Vec<VEC>::kWords; ++k) {
       const float2 a = unpack2<T>(g.w[k]);
-      const float2 b = unpack2<T>(u.w[k]);
-      o.w[k] = pack2<T>(activate<ACT>(a.x) * b.x, activate<ACT>(a.y) * b.y);
+      const float2 y = __fmul2_rn(make_float2(activate<ACT>(a.x), activate<ACT>(a.y)),
+                                  unpack2<T>(u.w[k]));
+      o.w[k] = pack2<T>(y.x, y.y);
     }
   }
   return o;
