@@ -28,11 +28,17 @@ BUILD = os.path.join(ROOT, "_build")
 LIB_NAME = "libhp_rms_norm_b200.so"
 LIB = os.path.join(PKG, LIB_NAME)
 CUDA_SOURCES = ["rms_norm.cu", "relu.cu", "act_and_mul.cu", "runtime.cu"]
-HEADERS = ["vec.cuh", "runtime.cuh"]
+HEADERS = ["vec.cuh", "bulk.cuh", "runtime.cuh"]
 
-# HPRN_DEBUG=1 builds host code without optimisation and with debug symbols
-# (device code keeps -O3 and -lineinfo, so kernels stay representative).
-DEBUG = os.environ.get("HPRN_DEBUG", "0") == "1"
+# HPRN_DEBUG=1 (or the reference's own DEBUG=1, setup.py:23-28 there) builds
+# host code without optimisation and with debug symbols (device code keeps -O3
+# and -lineinfo, so kernels stay representative).
+DEBUG = os.environ.get("HPRN_DEBUG", os.environ.get("DEBUG", "0")) == "1"
+# The reference's USE_CUDA=0 builds its extension without kernels; this
+# package is its CUDA kernels, so there is no such build.
+if os.environ.get("USE_CUDA", "1") == "0":
+    raise SystemExit("hp_rms_norm_b200 has no CPU-only build (USE_CUDA=0): it is CUDA kernels "
+                     "for sm_100a; unset USE_CUDA")
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
