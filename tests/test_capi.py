@@ -59,6 +59,42 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     assert capi.plan(4096, 1024) == "warp:vec32:vpt2:tpr32:cluster1:rpc8"
 
 
+@pytest.mark.parametrize("hidden,plan", [
+    # rows past one CTA: eight-CTA clusters, one vector per thread up to 512
+    # vectors per CTA, else two (the long-row sweep's fit)
+    (40960, "cluster:vec32:vpt1:tpr320:cluster8:rpc1"),
+    (65536, "cluster:vec32:vpt1:tpr512:cluster8:rpc1"),
+    (98304, "cluster:vec32:vpt2:tpr384:cluster8:rpc1"),
+    (131072, "cluster:vec32:vpt2:tpr512:cluster8:rpc1"),
+    (262144, "cluster:vec32:vpt2:tpr1024:cluster8:rpc1"),
+    (262160, "twopass:vec32:vpt4:tpr512:cluster1:rpc1"),
+    # the config-1 sweep's regimes
+    (20480, "cta:vec32:vpt4:tpr320:cluster1:rpc1"),
+    (24576, "cta:vec32:vpt2:tpr768:cluster1:rpc1"),
+    (32768, "cta:vec32:vpt2:tpr1024:cluster1:rpc1"),
+])
+def test_fitted_plans(hidden, plan):
+    assert capi.plan(4096, hidden) == plan
+
+
+def test_tuner_tma_candidates_fit_a_cta():
+    from hp_rms_norm_b200 import tune
+
+    for hidden, residual in ((1024, True), (4096, True), (16384, True), (16384, False)):
+        cands = tune.tma_candidates(hidden, residual)
+        assert cands, hidden
+        for c in cands:
+            f = dict(re.findall(r"([a-z]+)(\d+)", c))
+            vec, vpt, tpr, stages = (int(f[k]) for k in ("vec", "vpt", "tpr", "rpc"))
+            assert tpr * vpt * (vec // 2) >= hidden, c
+            assert stages * (2 if residual else 1) * hidden * 2 <= tune.TMA_SMEM, c
+            load = vpt * vec // 16
+            assert tpr <= (1024 if load <= 2 else 512 if load <= 4 else 256), c
+    # A fused row of 32768 is a 128 KB stage: one ring slot, 32-byte vectors only.
+    assert tune.tma_candidates(32768, True) == ["tma:vec32:vpt8:tpr256:cluster1:rpc1"]
+    assert tune.tma_candidates(65536, True) == []  # no CTA covers it
+
+
 def test_plan_vector_width_follows_alignment_and_hidden():
     assert ":vec32:" in capi.plan(8, 4096, input_ptr=256, residual_ptr=1 << 20)
     assert ":vec16:" in capi.plan(8, 4096, input_ptr=256 + 16, residual_ptr=1 << 20)
