@@ -164,6 +164,24 @@ __device__ __forceinline__ float vec_amax_rw(const Vec<VEC>& rv, const Vec<VEC>&
   return m;
 }
 
+// square_sum and vec_amax_rw over one input vector in one pass (plain rows
+// with a dynamic fp8 scale), unpacking each pair once for both.
+template <typename T, int VEC>
+__device__ __forceinline__ float square_sum_amax(const Vec<VEC>& xv, const Vec<VEC>& wv, float& a0,
+                                                 float& a1, float m) {
+  float2 acc = make_float2(a0, a1);
+#pragma unroll
+  for (int k = 0; k < Vec<VEC>::kWords; ++k) {
+    const float2 x = unpack2<T>(xv.w[k]);
+    acc = __ffma2_rn(x, x, acc);
+    const float2 p = __fmul2_rn(x, unpack2<T>(wv.w[k]));
+    m = fmaxf(m, fmaxf(fabsf(p.x), fabsf(p.y)));
+  }
+  a0 = acc.x;
+  a1 = acc.y;
+  return m;
+}
+
 // e4m3_satfinite((f32(r) * f32(w) * inv) * inv_scale) for one vector: VEC/2
 // output bytes, element order preserved.
 template <typename T, int VEC>
@@ -345,6 +363,10 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
     }
   }
   float a0 = 0.f, a1 = 0.f;
+  // Dynamic fp8: max |r * w| does not depend on inv, so it is reduced next to
+  // the sum of squares and scaled by inv once (see vec_amax_rw); plain rows
+  // take it in the same pass as the sum of squares.
+  float m = 0.f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = lane + 32 * j;
@@ -352,16 +374,15 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
       if constexpr (RES) {
         add_round<T, VEC>(xv[j], rv[j], a0, a1);
         st_global<VEC>(rr + v * EPV, xv[j]);
+      } else if constexpr (OUT == kOutFp8Dynamic) {
+        m = square_sum_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), a0, a1, m);
       } else {
         square_sum<T, VEC>(xv[j], a0, a1);
       }
       if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
     }
   }
-  // Dynamic fp8: max |r * w| does not depend on inv, so it is reduced next to
-  // the sum of squares and scaled by inv once (see vec_amax_rw).
-  float m = 0.f;
-  if constexpr (OUT == kOutFp8Dynamic) {
+  if constexpr (RES && OUT == kOutFp8Dynamic) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = lane + 32 * j;
@@ -441,7 +462,13 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
       if constexpr (RES) rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
     }
   }
+  // Dynamic fp8: max |r * w| does not depend on inv, so it travels with the
+  // sum of squares through the same barrier (and cluster phase) and is scaled
+  // by inv once at the end (see vec_amax_rw); plain rows take it in the same
+  // pass as the sum of squares.
+  constexpr bool kAmax = OUT == kOutFp8Dynamic;
   float a0 = 0.f, a1 = 0.f;
+  float m = 0.f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = v_begin + tid + j * nthreads;
@@ -449,19 +476,15 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
       if constexpr (RES) {
         add_round<T, VEC>(xv[j], rv[j], a0, a1);
         st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+      } else if constexpr (kAmax) {
+        m = square_sum_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), a0, a1, m);
       } else {
         square_sum<T, VEC>(xv[j], a0, a1);
       }
       if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
     }
   }
-
-  // Dynamic fp8: max |r * w| does not depend on inv, so it travels with the
-  // sum of squares through the same barrier (and cluster phase) and is scaled
-  // by inv once at the end (see vec_amax_rw).
-  constexpr bool kAmax = OUT == kOutFp8Dynamic;
-  float m = 0.f;
-  if constexpr (kAmax) {
+  if constexpr (RES && kAmax) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = v_begin + tid + j * nthreads;
