@@ -85,6 +85,8 @@ def candidates(nvec: int, full: bool = True) -> list[str]:
                 continue
             kind = "cta" if cl == 1 else "cluster"
             out.append(f"{kind}:vec32:vpt{vpt}:tpr{tpr}:cluster{cl}:rpc1")
+    if nvec > 8 * 2048:  # two passes, one CTA or a cluster per row
+        out += [f"twopass:vec32:vpt4:tpr{t}:cluster{cl}:rpc1" for cl in (1, 2, 4, 8) for t in (256, 512)]
     return out
 
 

@@ -67,7 +67,7 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     (98304, "cluster:vec32:vpt2:tpr384:cluster8:rpc1"),
     (131072, "cluster:vec32:vpt2:tpr512:cluster8:rpc1"),
     (262144, "cluster:vec32:vpt2:tpr1024:cluster8:rpc1"),
-    (262160, "twopass:vec32:vpt4:tpr512:cluster1:rpc1"),
+    (262160, "twopass:vec32:vpt4:tpr256:cluster8:rpc1"),
     # the config-1 sweep's regimes
     (20480, "cta:vec32:vpt4:tpr320:cluster1:rpc1"),
     (24576, "cta:vec32:vpt2:tpr768:cluster1:rpc1"),

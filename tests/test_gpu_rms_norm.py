@@ -123,6 +123,10 @@ FORCED = [
     (9, 4096, "cta:vec4:vpt8:tpr256:cluster1:rpc1"),
     (9, 4096, "cluster:vec2:vpt8:tpr128:cluster4:rpc1"),
     (9, 4096, "twopass:vec2:vpt4:tpr512:cluster1:rpc1"),
+    (9, 8192, "twopass:vec32:vpt4:tpr256:cluster2:rpc1"),
+    (7, 20000, "twopass:vec32:vpt4:tpr128:cluster4:rpc1"),
+    (5, 1 << 19, "twopass:vec32:vpt4:tpr512:cluster8:rpc1"),
+    (9, 4097, "twopass:vec2:vpt4:tpr512:cluster4:rpc1"),
     (33, 256, "warp:vec16:vpt1:tpr32:cluster1:rpc8"),
     (33, 256, "warp:vec4:vpt4:tpr32:cluster1:rpc3"),
 ]
