@@ -100,6 +100,22 @@ def test_config4_full_shapes_vs_torch_fp32(cuda, rows, hidden):
     del want_out, want_res
 
 
+@pytest.mark.parametrize("rows,hidden,offset", [(2, 1 << 27, 0), (3, (1 << 26) + 7, 1)])
+def test_longest_rows_vs_torch_fp32(cuda, rows, hidden, offset):
+    """Rows of 2^26-2^27 elements (the clustered two-pass kernel, 32-bit vector
+    indices far past any other case): 32-byte vectors, and an odd hidden size
+    at a 2-byte offset (2-byte vectors, 2^26 of them per row)."""
+    x, w, r, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=hidden, device=cuda)
+    if offset:
+        x = torch.empty(rows * hidden + offset, dtype=x.dtype, device=cuda)[offset:].view(rows, hidden).copy_(x)
+    assert capi.plan(rows, hidden, capi.DTYPE_BF16, x.data_ptr(), r.data_ptr()).startswith("twopass")
+    want_out, want_res = torch_fp32_reference(x, w, r, eps)
+    run_capi(x, w, r, eps)
+    assert torch.equal(r.view(torch.int16), want_res.view(torch.int16))
+    assert int(ulp_distance(x, want_out).max()) <= 1
+    del want_out, want_res
+
+
 # Plans forced through the tuning hook: every kernel kind, vector width,
 # vectors-per-thread and cluster size the library compiles.
 FORCED = [
