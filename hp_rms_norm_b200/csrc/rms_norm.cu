@@ -32,8 +32,9 @@
 //     whose partial sums meet in distributed shared memory, so that CTAs stay
 //     small enough for many to be resident per SM at every hidden size (no
 //     occupancy cliff at large hidden);
-//   * rows too long for the register-resident kernels use a two-pass kernel
-//     that re-reads its own just-written residual from L2, not HBM;
+//   * rows too long for the register-resident kernels use a two-pass kernel,
+//     each row split over an eight-CTA cluster, that re-reads its own
+//     just-written residual (mostly from L2);
 //   * a fifth kernel stages rows in shared memory with TMA bulk copies and
 //     mbarriers (plan kind "tma").  Timed against the register-resident
 //     kernels at every shape, it is never faster on the fused form, so the
@@ -774,7 +775,7 @@ struct Plan {
   int vpt = 1;           // vectors per thread
   int tpr = 32;          // threads per CTA working on one row slice
   int cluster = 1;       // CTAs per row
-  int rows_per_cta = 1;  // warp kind only
+  int rows_per_cta = 1;  // warp kind: rows per CTA; tma kind: ring depth (rows in flight per CTA)
 };
 
 // Kernel family of one call: residual or not, and the output form.
@@ -855,8 +856,8 @@ int extended_vpt(int nvec, bool residual, int out) {
   }
 }
 
-// Every plan default_plan returns is compiled for every variant, except two
-// passes (rows past 8 * 2048 vectors), which only the 16-bit outputs have.
+// Every plan default_plan returns is compiled for the variant it is returned
+// for; two passes (rows past 8 * 2048 vectors) exist for 16-bit outputs only.
 Plan default_plan(int nvec, int vec, bool residual, int out) {
   Plan p;
   p.vec = vec;
