@@ -13,6 +13,6 @@ import torch
 from . import _C  # noqa: F401  (registers torch.ops.hp_rms_norm.*)
 from .ops import *  # noqa: F401,F403
 from .ops import (fused_add_rms_norm, gelu_and_mul, gelu_tanh_and_mul, hp_rms_norm, relu,
-                  rms_norm, rms_norm_fp8, rms_norm_nvfp4, silu_and_mul)
+                  rms_norm, rms_norm_fp8, rms_norm_fp8_group, rms_norm_nvfp4, silu_and_mul)
 
 __version__ = "1.0.0"

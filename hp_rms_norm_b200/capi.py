@@ -33,6 +33,7 @@ OUT_SAME = 0
 OUT_FP8_E4M3_STATIC = 1
 OUT_FP8_E4M3_DYNAMIC = 2
 OUT_NVFP4 = 3
+OUT_FP8_E4M3_GROUP = 4
 
 # Every symbol include/hp_rms_norm_b200.h declares.
 EXPORTED = (
@@ -49,6 +50,7 @@ EXPORTED = (
     "hprn_rms_norm_plan",
     "hprn_set_plan_override",
     "hprn_wait_timeouts",
+    "hprn_rms_norm_fp8_group",
 )
 
 
@@ -101,6 +103,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_set_plan_override.restype = c_int
     lib.hprn_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint), c_int]
     lib.hprn_wait_timeouts.restype = c_int
+    lib.hprn_rms_norm_fp8_group.argtypes = [vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64, i64,
+                                            ctypes.c_double, c_int, c_int, c_int, vp, u32]
+    lib.hprn_rms_norm_fp8_group.restype = c_int
     _lib = lib
     return lib
 
@@ -156,6 +161,19 @@ def rms_norm_nvfp4(out_ptr: int, block_scales_ptr: int, input_ptr: int, weight_p
                                       residual_ptr, rows, hidden, out_row_stride, input_row_stride,
                                       residual_row_stride, eps, dtype, global_scale_ptr, stream,
                                       flags))
+
+
+def rms_norm_fp8_group(out_ptr: int, scales_ptr: int, scale_row_stride: int,
+                       scale_group_stride: int, input_ptr: int, weight_ptr: int,
+                       residual_ptr: int | None, rows: int, hidden: int, out_row_stride: int,
+                       input_row_stride: int, residual_row_stride: int, eps: float, dtype: int,
+                       group_size: int = 128, scale_pow2: bool = False, stream: int = 0,
+                       flags: int = LAUNCH_DEFAULT) -> None:
+    _check(load().hprn_rms_norm_fp8_group(out_ptr, scales_ptr, scale_row_stride,
+                                          scale_group_stride, input_ptr, weight_ptr, residual_ptr,
+                                          rows, hidden, out_row_stride, input_row_stride,
+                                          residual_row_stride, eps, dtype, group_size,
+                                          1 if scale_pow2 else 0, stream, flags))
 
 
 def act_and_mul(out_ptr: int, input_ptr: int, rows: int, d: int, out_row_stride: int,
@@ -255,6 +273,24 @@ def act_and_mul_tensors(out, inp, act: int, stream: int | None = None,
     rows, d = out.shape
     act_and_mul(out.data_ptr(), inp.data_ptr(), rows, d, out.stride(0), inp.stride(0), act,
                 dtype_code(inp), stream, flags)
+
+
+def rms_norm_fp8_group_tensors(out, scales, inp, weight, res, eps: float, group_size: int = 128,
+                               scale_pow2: bool = False, stream: int | None = None,
+                               flags: int = LAUNCH_DEFAULT) -> None:
+    """hprn_rms_norm_fp8_group on 2-D CUDA tensors: out float8_e4m3fn / uint8
+    [rows, hidden], scales float32 [rows, hidden / group_size] with any strides
+    (row-major, or a transposed view for column-major scales)."""
+    import torch
+
+    if stream is None:
+        stream = torch.cuda.current_stream(inp.device).cuda_stream
+    rows, hidden = inp.shape
+    rms_norm_fp8_group(out.data_ptr(), scales.data_ptr(), scales.stride(0), scales.stride(1),
+                       inp.data_ptr(), weight.data_ptr(), res.data_ptr() if res is not None else None,
+                       rows, hidden, out.stride(0), inp.stride(0),
+                       res.stride(0) if res is not None else hidden, eps, dtype_code(inp),
+                       group_size, scale_pow2, stream, flags)
 
 
 def rms_norm_nvfp4_tensors(out, block_scales, inp, weight, res, eps: float, global_scale,

@@ -62,7 +62,8 @@ enum OutForm : int {
   kOutSame = HPRN_OUT_SAME,                   // 16-bit T into `out` (may be the input)
   kOutFp8Static = HPRN_OUT_FP8_E4M3_STATIC,   // e4m3 with one scale for the tensor
   kOutFp8Dynamic = HPRN_OUT_FP8_E4M3_DYNAMIC,  // e4m3 with one scale per row, written out
-  kOutNvfp4 = HPRN_OUT_NVFP4  // e2m1 pairs + one e4m3 scale per 16 elements (NVFP4)
+  kOutNvfp4 = HPRN_OUT_NVFP4,  // e2m1 pairs + one e4m3 scale per 16 elements (NVFP4)
+  kOutFp8Group = HPRN_OUT_FP8_E4M3_GROUP  // e4m3 with one scale per group of a row, written out
 };
 
 constexpr float kE4m3Max = 448.0f;
@@ -85,6 +86,12 @@ struct RmsArgs {
   int32_t rows_per_cta;
   float eps;
   float inv_hidden;
+  // Per-group fp8 scales (in row_scales): the scale of row i, group g sits
+  // at i * gs_row + g * gs_group; a group is group_vecs vectors.
+  int64_t gs_row;
+  int64_t gs_group;
+  int32_t group_vecs;
+  int32_t scale_pow2;  // round group scales up to powers of two
 };
 
 // Element pairs go through Blackwell's packed fp32 instructions
@@ -338,6 +345,39 @@ __device__ __forceinline__ Vec<VEC> weight_vec(const RmsArgs& a, int64_t v, cons
   return ld_weight<VEC>(a.w + v * Vec<VEC>::kElems, pol_keep);
 }
 
+// The smallest power of two >= s, for a positive normal float s (exact: the
+// exponent field goes up by one unless the mantissa field is zero).
+__device__ __forceinline__ float pow2_ceil(float s) {
+  uint32_t u = __float_as_uint(s);
+  if (u & 0x7fffffu) u = (u & 0xff800000u) + 0x800000u;
+  return __uint_as_float(u);
+}
+
+// Per-token-group fp8 for output vector v (in: v is inside the row slice).
+// The vectors of one group sit in group_vecs consecutive lanes of a warp
+// (vector index = a group-aligned base + lane), so the group amax is a
+// butterfly over log2(group_vecs) lanes: every lane of the warp must call
+// this, lanes outside the slice with in = false.  max |y| over a vector is
+// max |r * w| times inv, rounded once (exact, see vec_amax_rw).
+template <typename T, int VEC, bool RES>
+__device__ __forceinline__ void store_group_fp8(const RmsArgs& a, int64_t row, int v, bool in,
+                                                const Vec<VEC>& rv, const Vec<VEC>& held,
+                                                float inv, uint64_t pol_keep) {
+  constexpr int EPV = Vec<VEC>::kElems;
+  Vec<VEC> wv = held;
+  if (!RES && in) wv = weight_vec<VEC, RES>(a, v, held, pol_keep);
+  float m = in ? vec_amax_rw<T, VEC>(rv, wv, 0.f) * inv : 0.f;
+  for (int o = 1; o < a.group_vecs; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float scale = fmaxf(m, kMinAmax) / kE4m3Max;
+  if (a.scale_pow2) scale = pow2_ceil(scale);
+  if (in) {
+    uint8_t* o = static_cast<uint8_t*>(a.out) + row * a.out_stride + static_cast<int64_t>(v) * EPV;
+    st_global<VEC / 2>(o, quantize_e4m3<T, VEC>(rv, wv, inv, 1.0f / scale));
+    if (v % a.group_vecs == 0)
+      a.row_scales[row * a.gs_row + static_cast<int64_t>(v / a.group_vecs) * a.gs_group] = scale;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 1: one warp per row (rows of at most 4 * 32 vectors).  No shared
 // memory, no block barrier: a warp that has finished its row retires without
@@ -400,9 +440,12 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = lane + 32 * j;
-    if (v < a.nvec)
+    if constexpr (OUT == kOutFp8Group) {
+      store_group_fp8<T, VEC, RES>(a, row, v, v < a.nvec, xv[j], wv[j], inv, pol_keep);
+    } else if (v < a.nvec) {
       store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
                              inv_scale);
+    }
   }
 }
 
@@ -523,9 +566,12 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int v = v_begin + tid + j * nthreads;
-    if (v < v_end)
+    if constexpr (OUT == kOutFp8Group) {
+      store_group_fp8<T, VEC, RES>(a, row, v, v < v_end, xv[j], wv[j], inv, pol_keep);
+    } else if (v < v_end) {
       store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
                              inv_scale);
+    }
   }
 }
 
@@ -829,6 +875,14 @@ bool vpt_supported(Kind k, int vec, int vpt, const Variant& v) {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+// Vectors per cluster CTA: the row split evenly, rounded up to whole groups
+// (8 vectors, a multiple of every group size) for per-group fp8 output so a
+// group never straddles two CTAs.
+int slice_vecs_of(int nvec, int cluster, int out) {
+  const int slice = (nvec + cluster - 1) / cluster;
+  return out == kOutFp8Group && cluster > 1 ? (slice + 7) / 8 * 8 : slice;
+}
+
 // Launch-plan heuristic, fitted to a cold-L2 sweep of every compiled plan on
 // B200 (batch 4096 bf16, hidden 1024..32768; the kernel timed as back-to-back
 // CUDA-graph launches over rotating buffers).  What won everywhere:
@@ -851,7 +905,8 @@ int extended_vpt(int nvec, bool residual, int out) {
   switch (out) {
     case kOutSame: return nvec <= 128 ? 0 : (nvec <= 256 ? 1 : 2);
     case kOutFp8Static: return nvec <= 128 ? 0 : (nvec <= 1024 ? 2 : 4);
-    case kOutFp8Dynamic: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
+    case kOutFp8Dynamic:
+    case kOutFp8Group: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
     default: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);  // NVFP4 (past 1536: a cluster)
   }
 }
@@ -920,7 +975,7 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
     p.kind = kClusterRows;
     p.vpt = residual ? 2 : 4;
     p.cluster = residual ? 8 : (nvec < 4096 ? 4 : 8);
-    const int slice = (nvec + p.cluster - 1) / p.cluster;
+    const int slice = slice_vecs_of(nvec, p.cluster, out);
     p.tpr = round_up((slice + p.vpt - 1) / p.vpt, 32);
     return p;
   }
@@ -1012,7 +1067,7 @@ bool plan_valid(const Plan& p, int nvec, int max_vec, const Variant& var, std::s
         *why = "cluster must be 1..8 and tpr a multiple of 32 within the kernel's launch bound";
         return false;
       }
-      const int slice = (nvec + c - 1) / c;
+      const int slice = slice_vecs_of(nvec, c, var.out);
       if (static_cast<int64_t>(p.tpr) * p.vpt < slice) {
         *why = "tpr * vpt does not cover the row slice";
         return false;
@@ -1106,7 +1161,7 @@ KernelFn pick_kind(const Plan& p) {
 
 template <typename T, bool RES, int OUT>
 KernelFn pick_vec(const Plan& p) {
-  if constexpr (OUT == kOutNvfp4) {
+  if constexpr (OUT == kOutNvfp4 || OUT == kOutFp8Group) {
     return p.vec == 32 ? pick_kind<T, 32, RES, OUT>(p) : nullptr;
   } else if constexpr (OUT == kOutSame) {
     switch (p.vec) {
@@ -1133,6 +1188,7 @@ KernelFn pick_variant(const Plan& p, const Variant& v) {
       case kOutSame: return pick_vec<T, true, kOutSame>(p);
       case kOutFp8Static: return pick_vec<T, true, kOutFp8Static>(p);
       case kOutNvfp4: return pick_vec<T, true, kOutNvfp4>(p);
+      case kOutFp8Group: return pick_vec<T, true, kOutFp8Group>(p);
       default: return pick_vec<T, true, kOutFp8Dynamic>(p);
     }
   }
@@ -1140,6 +1196,7 @@ KernelFn pick_variant(const Plan& p, const Variant& v) {
     case kOutSame: return pick_vec<T, false, kOutSame>(p);
     case kOutFp8Static: return pick_vec<T, false, kOutFp8Static>(p);
     case kOutNvfp4: return pick_vec<T, false, kOutNvfp4>(p);
+    case kOutFp8Group: return pick_vec<T, false, kOutFp8Group>(p);
     default: return pick_vec<T, false, kOutFp8Dynamic>(p);
   }
 }
@@ -1162,13 +1219,19 @@ struct Problem {
   int dtype;
   int out_form;
   const float* scale;
-  float* row_scales;
+  float* row_scales;  // per-row fp8 scales, or the per-group scales
   uint8_t* block_scales;
+  int64_t gs_row = 0, gs_group = 0;  // per-group scale strides (floats)
+  int group_size = 0;
+  int scale_pow2 = 0;
 };
 
 int out_elem_bytes(const Problem& q) { return q.out_form == kOutSame ? 2 : 1; }
 
-bool is_fp8(const Problem& q) { return q.out_form == kOutFp8Static || q.out_form == kOutFp8Dynamic; }
+bool is_fp8(const Problem& q) {
+  return q.out_form == kOutFp8Static || q.out_form == kOutFp8Dynamic || q.out_form == kOutFp8Group;
+}
+
 
 // [first, last) byte range of `rows` rows of `hidden` elements at `stride`.
 struct Span {
@@ -1199,7 +1262,7 @@ int validate(const Problem& q) {
   if (q.dtype != HPRN_DTYPE_BF16 && q.dtype != HPRN_DTYPE_FP16)
     return fail(HPRN_ERR_UNSUPPORTED_DTYPE, "dtype must be kFloat16 or kBFloat16");
   if (q.out_form != kOutSame && q.out_form != kOutFp8Static && q.out_form != kOutFp8Dynamic &&
-      q.out_form != kOutNvfp4)
+      q.out_form != kOutNvfp4 && q.out_form != kOutFp8Group)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "unknown output form");
   if (q.rows < 0) return fail(HPRN_ERR_INVALID_ARGUMENT, "rows must be >= 0");
   if (q.hidden < 1 || q.hidden > (static_cast<int64_t>(1) << 30))
@@ -1212,6 +1275,18 @@ int validate(const Problem& q) {
     return fail(HPRN_ERR_INVALID_ARGUMENT, "dynamic fp8 output needs a row_scales buffer");
   if (q.out_form == kOutNvfp4 && (!q.scale || !q.block_scales))
     return fail(HPRN_ERR_INVALID_ARGUMENT, "NVFP4 output needs a global scale and a block_scales buffer");
+  if (q.out_form == kOutFp8Group) {
+    if (!q.row_scales)
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "per-group fp8 output needs a scales buffer");
+    if (q.group_size != 32 && q.group_size != 64 && q.group_size != 128)
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "group_size must be 32, 64 or 128");
+    if (q.hidden % q.group_size)
+      return fail(HPRN_ERR_INVALID_ARGUMENT, "hidden_dim must be a multiple of group_size");
+    if (q.gs_row < 0 || q.gs_group < 0 || (q.rows > 1 && q.gs_row == 0) ||
+        (q.hidden > q.group_size && q.gs_group == 0))
+      return fail(HPRN_ERR_INVALID_ARGUMENT,
+                  "scale strides must be positive (one scale slot per row and group)");
+  }
   if (q.out_form == kOutNvfp4 && (q.hidden % 16 || (q.rows > 1 && q.os % 16)))
     return fail(HPRN_ERR_INVALID_ARGUMENT,
                 "NVFP4 output needs hidden_dim % 16 == 0 and an output row stride that is a "
@@ -1248,6 +1323,13 @@ int validate(const Problem& q) {
 
 // Largest vector width every pointer, stride and the hidden size allow.
 int choose_vec(const Problem& q) {
+  if (q.out_form == kOutFp8Group) {
+    const bool ok = q.hidden % 16 == 0 && aligned(q.x, 32) && aligned(q.w, 32) &&
+                    (!q.r || aligned(q.r, 32)) && aligned(q.out, 16) &&
+                    (q.rows <= 1 || ((q.xs * 2) % 32 == 0 && (!q.r || (q.rs * 2) % 32 == 0) &&
+                                     q.os % 16 == 0));
+    return ok ? 32 : 0;
+  }
   if (q.out_form == kOutNvfp4) {
     const bool ok = q.hidden % 16 == 0 && aligned(q.x, 32) && aligned(q.w, 32) &&
                     (!q.r || aligned(q.r, 32)) && aligned(q.out, 8) &&
@@ -1276,6 +1358,10 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
     return fail(HPRN_ERR_INVALID_ARGUMENT,
                 "NVFP4 output needs 32-byte aligned input/weight/residual rows and 8-byte aligned "
                 "output rows");
+  if (q.out_form == kOutFp8Group && max_vec != 32)
+    return fail(HPRN_ERR_INVALID_ARGUMENT,
+                "per-group fp8 output needs 32-byte aligned input/weight/residual rows and "
+                "16-byte aligned output rows");
   if (is_fp8(q) && max_vec < 8)
     return fail(HPRN_ERR_INVALID_ARGUMENT,
                 "fp8 output needs hidden_dim % 4 == 0 and 8-byte aligned input/weight/residual "
@@ -1309,10 +1395,14 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   a.r_stride = q.rs;
   a.out_stride = q.os;
   a.nvec = static_cast<int>(q.hidden / epv);
-  a.slice_vecs = (a.nvec + p.cluster - 1) / p.cluster;
+  a.slice_vecs = slice_vecs_of(a.nvec, p.cluster, var.out);
   a.rows_per_cta = p.rows_per_cta;
   a.eps = static_cast<float>(q.eps);
   a.inv_hidden = 1.0f / static_cast<float>(q.hidden);
+  a.gs_row = q.gs_row;
+  a.gs_group = q.gs_group;
+  a.group_vecs = q.out_form == kOutFp8Group ? q.group_size / epv : 1;
+  a.scale_pow2 = q.scale_pow2 != 0;
   *plan = p;
   *args = a;
   return HPRN_OK;
@@ -1399,7 +1489,7 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
     c.out = static_cast<char*>(a.out) + (var.out == kOutSame    ? out_elems * 2
                                          : var.out == kOutNvfp4 ? out_elems / 2
                                                                 : out_elems);
-    if (a.row_scales) c.row_scales = a.row_scales + done;
+    if (a.row_scales) c.row_scales = a.row_scales + done * (var.out == kOutFp8Group ? a.gs_row : 1);
     if (a.block_scales) c.block_scales = a.block_scales + done * a.nvec;
     c.rows = n;
     const int64_t units = (n + rows_per_unit - 1) / rows_per_unit;
@@ -1479,6 +1569,9 @@ int hprn_rms_norm_out(void* out, const void* input, const void* weight, void* re
   using namespace hprn;
   if (out_form == HPRN_OUT_NVFP4)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "NVFP4 output goes through hprn_rms_norm_nvfp4");
+  if (out_form == HPRN_OUT_FP8_E4M3_GROUP)
+    return fail(HPRN_ERR_INVALID_ARGUMENT,
+                "per-group fp8 output goes through hprn_rms_norm_fp8_group");
   Problem q{out, input, weight, residual, rows, hidden, out_row_stride, input_row_stride,
             residual_row_stride, eps, dtype, out_form, scale, row_scales, nullptr};
   return run(q, stream, flags);
@@ -1491,6 +1584,19 @@ int hprn_rms_norm_nvfp4(void* out, uint8_t* block_scales, const void* input, con
   using namespace hprn;
   Problem q{out, input, weight, residual, rows, hidden, out_row_stride, input_row_stride,
             residual_row_stride, eps, dtype, kOutNvfp4, global_scale, nullptr, block_scales};
+  return run(q, stream, flags);
+}
+
+int hprn_rms_norm_fp8_group(void* out, float* scales, int64_t scale_row_stride,
+                            int64_t scale_group_stride, const void* input, const void* weight,
+                            void* residual, int64_t rows, int64_t hidden, int64_t out_row_stride,
+                            int64_t input_row_stride, int64_t residual_row_stride, double eps,
+                            int dtype, int group_size, int scale_pow2, void* stream,
+                            unsigned flags) {
+  using namespace hprn;
+  Problem q{out, input, weight, residual, rows, hidden, out_row_stride, input_row_stride,
+            residual_row_stride, eps, dtype, kOutFp8Group, nullptr, scales, nullptr,
+            scale_row_stride, scale_group_stride, group_size, scale_pow2};
   return run(q, stream, flags);
 }
 

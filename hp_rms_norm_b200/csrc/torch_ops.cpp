@@ -265,6 +265,33 @@ void rms_norm_nvfp4(at::Tensor& out, at::Tensor& block_scales, const at::Tensor&
                                    HPRN_LAUNCH_DEFAULT));
 }
 
+// Per-token-group fp8 output (extension past the reference): out
+// float8_e4m3fn [..., hidden]; scales float32 [rows, hidden / group_size]
+// (rows = the input's leading dimensions flattened), any strides, so a
+// transposed view gives column-major scales.
+void rms_norm_fp8_group(at::Tensor& out, at::Tensor& scales, const at::Tensor& input,
+                        const at::Tensor& weight, c10::optional<at::Tensor> residual, double eps,
+                        int64_t group_size, bool scale_pow2) {
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn, "out must be float8_e4m3fn");
+  const OutCall c = check_out_call(out, input, weight, residual);
+  TORCH_CHECK(group_size == 32 || group_size == 64 || group_size == 128,
+              "group_size must be 32, 64 or 128");
+  TORCH_CHECK(c.hidden % group_size == 0, "hidden_dim must be a multiple of group_size");
+  TORCH_CHECK(scales.scalar_type() == at::kFloat && scales.dim() == 2 &&
+                  scales.size(0) == c.rows && scales.size(1) == c.hidden / group_size,
+              "scales must be float32 [rows, hidden / group_size]");
+  TORCH_CHECK(scales.is_cuda() && scales.device() == input.device(),
+              "scales must be on the input's device");
+  if (c.rows == 0 || c.hidden == 0) return;
+  const c10::cuda::CUDAGuard guard(input.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
+  check_status(hprn_rms_norm_fp8_group(
+      out.data_ptr(), scales.data_ptr<float>(), scales.stride(0), scales.stride(1),
+      input.data_ptr(), weight.data_ptr(), residual.has_value() ? residual->data_ptr() : nullptr,
+      c.rows, c.hidden, c.os, c.xs, c.rs, eps, c.dtype, static_cast<int>(group_size),
+      scale_pow2 ? 1 : 0, stream, HPRN_LAUNCH_DEFAULT));
+}
+
 // out[..., d] = act(input[..., :d]) * input[..., d:]  (extension past the reference).
 void act_and_mul(at::Tensor& out, const at::Tensor& input, int act) {
   TORCH_CHECK(input.dim() >= 1 && input.size(-1) % 2 == 0, "input.size(-1) must be even");
@@ -307,6 +334,8 @@ void rms_norm_fp8_meta(at::Tensor&, const at::Tensor&, const at::Tensor&,
 void act_and_mul_meta(at::Tensor&, const at::Tensor&) {}
 void rms_norm_nvfp4_meta(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&,
                          c10::optional<at::Tensor>, double, const at::Tensor&) {}
+void rms_norm_fp8_group_meta(at::Tensor&, at::Tensor&, const at::Tensor&, const at::Tensor&,
+                             c10::optional<at::Tensor>, double, int64_t, bool) {}
 
 }  // namespace
 
@@ -321,6 +350,8 @@ TORCH_LIBRARY(hp_rms_norm, m) {
         "float eps, Tensor? scale, Tensor(c!)? row_scales) -> ()");
   m.def("rms_norm_nvfp4(Tensor(a!) out, Tensor(b!) block_scales, Tensor input, Tensor weight, "
         "Tensor(c!)? residual, float eps, Tensor global_scale) -> ()");
+  m.def("rms_norm_fp8_group(Tensor(a!) out, Tensor(b!) scales, Tensor input, Tensor weight, "
+        "Tensor(c!)? residual, float eps, int group_size, bool scale_pow2) -> ()");
   // Extensions: gated activations.
   m.def("silu_and_mul(Tensor(a!) out, Tensor input) -> ()");
   m.def("gelu_and_mul(Tensor(a!) out, Tensor input) -> ()");
@@ -333,6 +364,7 @@ TORCH_LIBRARY_IMPL(hp_rms_norm, CUDA, m) {
   m.impl("rms_norm_out", &rms_norm_out);
   m.impl("rms_norm_fp8", &rms_norm_fp8);
   m.impl("rms_norm_nvfp4", &rms_norm_nvfp4);
+  m.impl("rms_norm_fp8_group", &rms_norm_fp8_group);
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("gelu_and_mul", &gelu_and_mul);
   m.impl("gelu_tanh_and_mul", &gelu_tanh_and_mul);
@@ -344,6 +376,7 @@ TORCH_LIBRARY_IMPL(hp_rms_norm, Meta, m) {
   m.impl("rms_norm_out", &rms_norm_out_meta);
   m.impl("rms_norm_fp8", &rms_norm_fp8_meta);
   m.impl("rms_norm_nvfp4", &rms_norm_nvfp4_meta);
+  m.impl("rms_norm_fp8_group", &rms_norm_fp8_group_meta);
   m.impl("silu_and_mul", &act_and_mul_meta);
   m.impl("gelu_and_mul", &act_and_mul_meta);
   m.impl("gelu_tanh_and_mul", &act_and_mul_meta);

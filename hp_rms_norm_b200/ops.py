@@ -82,6 +82,27 @@ def rms_norm_nvfp4(input, weight, eps, global_scale, residual=None):
     return codes, scales
 
 
+def rms_norm_fp8_group(input, weight, eps, residual=None, group_size=128, scale_pow2=False,
+                       column_major_scales=False):
+    """RMSNorm (fused with ``residual += input`` when a residual is given) with a
+    per-token-group fp8 output: returns (out, scales), out float8_e4m3fn
+    [..., hidden], scales float32 [rows, hidden / group_size] (rows = the
+    leading dimensions flattened) with out ~ y / scale per group of
+    ``group_size`` elements.  ``scale_pow2`` rounds scales up to powers of two;
+    ``column_major_scales`` returns a transposed view of a [hidden /
+    group_size, rows] buffer (the layout block-scaled FP8 GEMMs read)."""
+    h = input.shape[-1]
+    rows = input.numel() // h if h else 0
+    out = torch.empty(input.shape, dtype=torch.float8_e4m3fn, device=input.device)
+    if column_major_scales:
+        scales = torch.empty((h // group_size, rows), dtype=torch.float32, device=input.device).t()
+    else:
+        scales = torch.empty((rows, h // group_size), dtype=torch.float32, device=input.device)
+    torch.ops.hp_rms_norm.rms_norm_fp8_group.default(out, scales, input, weight, residual, eps,
+                                                     group_size, scale_pow2)
+    return out, scales
+
+
 def _act_and_mul(op, input, out):
     if out is None:
         out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), dtype=input.dtype,
@@ -106,4 +127,4 @@ def gelu_tanh_and_mul(input, out=None):
 
 
 __all__ = ["hp_rms_norm", "relu", "rms_norm", "fused_add_rms_norm", "rms_norm_fp8", "rms_norm_nvfp4",
-           "silu_and_mul", "gelu_and_mul", "gelu_tanh_and_mul", "torch"]
+           "rms_norm_fp8_group", "silu_and_mul", "gelu_and_mul", "gelu_tanh_and_mul", "torch"]

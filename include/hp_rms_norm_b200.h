@@ -57,7 +57,8 @@ typedef enum hprn_out_form {
   HPRN_OUT_SAME = 0,              /* 16-bit, the input's dtype */
   HPRN_OUT_FP8_E4M3_STATIC = 1,   /* fp8 e4m3 (OCP E4M3FN), one scale for the tensor */
   HPRN_OUT_FP8_E4M3_DYNAMIC = 2,  /* fp8 e4m3, one scale per row, written to row_scales */
-  HPRN_OUT_NVFP4 = 3              /* fp4 e2m1 + e4m3 block scales: hprn_rms_norm_nvfp4 only */
+  HPRN_OUT_NVFP4 = 3,             /* fp4 e2m1 + e4m3 block scales: hprn_rms_norm_nvfp4 only */
+  HPRN_OUT_FP8_E4M3_GROUP = 4     /* fp8 e4m3, one scale per group: hprn_rms_norm_fp8_group only */
 } hprn_out_form;
 
 /* Activations of hprn_act_and_mul. */
@@ -181,6 +182,29 @@ HPRN_API int hprn_rms_norm_nvfp4(void* out, uint8_t* block_scales, const void* i
                                  int64_t out_row_stride, int64_t input_row_stride,
                                  int64_t residual_row_stride, double eps, int dtype,
                                  const float* global_scale, void* stream, unsigned flags);
+
+/*
+ * The same row operation as hprn_rms_norm_out (residual optional) with a
+ * per-token-group fp8 output (an extension past the reference; the
+ * quantisation FP8 GEMMs with block-wise scales consume): for every group g of
+ * `group_size` consecutive elements of row i,
+ *   s_ig = max(max_{j in g} |y_ij|, 1e-12) / 448, rounded up to a power of two
+ *          when scale_pow2 != 0 (scales an exponent-only format can hold)
+ *   out[i, j] = e4m3_satfinite(y_ij * (1 / s_ig))
+ *   scales[i * scale_row_stride + g * scale_group_stride] = s_ig   (fp32)
+ * y_ij is the fp32 normalised value (not rounded to 16 bits first).  The
+ * scale strides are in floats: (hidden / group_size, 1) for row-major scales,
+ * (1, rows or more) for column-major.  group_size is 32, 64 or 128;
+ * hidden % group_size == 0; input/weight/residual rows 32-byte aligned,
+ * output rows 16-byte aligned; out_row_stride in bytes (fp8 elements).
+ */
+HPRN_API int hprn_rms_norm_fp8_group(void* out, float* scales, int64_t scale_row_stride,
+                                     int64_t scale_group_stride, const void* input,
+                                     const void* weight, void* residual, int64_t rows,
+                                     int64_t hidden, int64_t out_row_stride,
+                                     int64_t input_row_stride, int64_t residual_row_stride,
+                                     double eps, int dtype, int group_size, int scale_pow2,
+                                     void* stream, unsigned flags);
 
 /* Message for the last non-OK status returned on this thread ("" if none). */
 HPRN_API const char* hprn_last_error(void);

@@ -62,6 +62,9 @@ def _load():
         lib.oracle_rms_norm_nvfp4.argtypes = [ctypes.c_int, vp, vp, u16p, u16p, vp, i64, i64,
                                               ctypes.c_double, ctypes.c_float]
         lib.oracle_rms_norm_nvfp4.restype = None
+        lib.oracle_rms_norm_fp8_group.argtypes = [ctypes.c_int, vp, vp, u16p, u16p, vp, i64, i64,
+                                                  ctypes.c_double, ctypes.c_int, ctypes.c_int]
+        lib.oracle_rms_norm_fp8_group.restype = None
         _lib = lib
     return _lib
 
@@ -149,6 +152,24 @@ def rms_norm_nvfp4(dtype: int, x: np.ndarray, w: np.ndarray, eps: float, global_
                               None if rc is None else rc.ctypes.data, rows, hidden, float(eps),
                               float(global_scale))
     return out, sf, rc
+
+
+def rms_norm_fp8_group(dtype: int, x: np.ndarray, w: np.ndarray, eps: float, group: int = 128,
+                       pow2: bool = False, r: np.ndarray | None = None):
+    """Per-token-group fp8 output of the row op: returns (e4m3 codes
+    [rows, hidden] uint8, scales [rows, hidden/group] float32, residual or None)."""
+    lib = _load()
+    hidden = x.shape[-1]
+    xc = np.ascontiguousarray(x, dtype=np.uint16)
+    rows = xc.size // hidden
+    rc = None if r is None else np.ascontiguousarray(r, dtype=np.uint16).copy()
+    out = np.empty((rows, hidden), dtype=np.uint8)
+    sc = np.empty((rows, hidden // group), dtype=np.float32)
+    lib.oracle_rms_norm_fp8_group(dtype, out.ctypes.data, sc.ctypes.data, _u16(xc),
+                                  _u16(np.ascontiguousarray(w, dtype=np.uint16)),
+                                  None if rc is None else rc.ctypes.data, rows, hidden, float(eps),
+                                  int(group), 1 if pow2 else 0)
+    return out, sc, rc
 
 
 ACTS = {"silu": 0, "gelu": 1, "gelu_tanh": 2}

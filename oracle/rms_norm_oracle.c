@@ -230,6 +230,57 @@ void oracle_rms_norm_out(int dtype, void* out, const uint16_t* input, const uint
   }
 }
 
+/* Per-token-group fp8: the row op of oracle_rms_norm_out (residual optional),
+ * then for each group g of `group` consecutive elements of a row
+ *   s_g = max(max_j |y_j|, 1e-12) / 448, rounded up to a power of two if pow2
+ *   q_j = e4m3_satfinite(y_j * (1 / s_g))
+ * y_j = (v_j * w_j) * inv in fp32 (v the rounded residual or the input), as
+ * in the other outputs.  out: rows x hidden bytes; scales: rows x hidden/group
+ * floats, row-major.  Fixes the semantics of the library's
+ * hprn_rms_norm_fp8_group (no reference counterpart). */
+static float pow2_ceil_f(float s) {
+  int e;
+  float m = frexpf(s, &e); /* s = m * 2^e, m in [0.5, 1) */
+  return m == 0.5f ? s : ldexpf(1.0f, e);
+}
+
+void oracle_rms_norm_fp8_group(int dtype, uint8_t* out, float* scales, const uint16_t* input,
+                               const uint16_t* weight, uint16_t* residual, int64_t rows,
+                               int64_t hidden, double eps, int group, int pow2) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < rows; ++i) {
+    const uint16_t* x = input + i * hidden;
+    uint16_t* r = residual ? residual + i * hidden : 0;
+    double ss = 0.0;
+    float* y = (float*)malloc(sizeof(float) * (size_t)hidden);
+    for (int64_t j = 0; j < hidden; ++j) {
+      float s = to_f32(dtype, x[j]);
+      if (r) {
+        s = s + to_f32(dtype, r[j]);
+        r[j] = from_f32(dtype, s);
+        y[j] = to_f32(dtype, r[j]);
+      } else {
+        y[j] = s;
+      }
+      ss += (double)s * (double)s;
+    }
+    float inv = (float)(1.0 / sqrt(ss / (double)hidden + eps));
+    for (int64_t j = 0; j < hidden; ++j) y[j] = y[j] * to_f32(dtype, weight[j]) * inv;
+    const int64_t ngroups = hidden / group;
+    for (int64_t g = 0; g < ngroups; ++g) {
+      float amax = 0.0f;
+      for (int64_t j = g * group; j < (g + 1) * group; ++j) amax = fmaxf(amax, fabsf(y[j]));
+      float sc = fmaxf(amax, 1e-12f) / 448.0f;
+      if (pow2) sc = pow2_ceil_f(sc);
+      scales[i * ngroups + g] = sc;
+      const float inv_scale = 1.0f / sc;
+      for (int64_t j = g * group; j < (g + 1) * group; ++j)
+        out[i * hidden + j] = f32_to_e4m3_satfinite(y[j] * inv_scale);
+    }
+    free(y);
+  }
+}
+
 /* ---- fp4 e2m1 (values 0, 0.5, 1, 1.5, 2, 3, 4, 6; no inf/NaN) -------------
  * Round to nearest even, saturating to +-6, from the format definition:
  * sign bit 3, two exponent bits (bias 1), one mantissa bit; exponent 0 is the

@@ -103,3 +103,41 @@ def test_nvfp4_dequantises_within_half_a_step(residual):
     assert np.all(np.abs(deq - y) <= bound)
     amax = np.abs(y).max(axis=-1)
     np.testing.assert_allclose(sfv, gs * amax / 6.0, rtol=2 ** -3)
+
+
+@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("group", [32, 64, 128])
+def test_fp8_group_is_the_dynamic_scale_per_group(residual, group):
+    """Per-token-group fp8: each group takes the per-row dynamic form's scale
+    rule (max |y| / 448 with a 1e-12 floor, then e4m3 of y times the inverse
+    scale) over its own elements, with the row's inverse RMS; y rebuilt here in
+    numpy from the definition, e4m3 from the conversion pinned to torch."""
+    x, w, r = _inputs(5, 512, O.BF16, 7)
+    rr = r if residual else None
+    q, sc, res = O.rms_norm_fp8_group(O.BF16, x, w, 1e-6, group=group, r=rr)
+    assert q.shape == (5, 512) and sc.shape == (5, 512 // group)
+    _, res16, _ = O.rms_norm_out(O.BF16, x, w, 1e-6, r=rr)
+    if residual:
+        assert_bits_equal(res, res16, O.BF16)
+    sums = O.to_f32(O.BF16, x) + (O.to_f32(O.BF16, r) if residual else np.float32(0))
+    inv = (1.0 / np.sqrt((sums.astype(np.float64) ** 2).sum(-1) / 512 + 1e-6)).astype(np.float32)
+    v = O.to_f32(O.BF16, res16 if residual else x)
+    y = (v * O.to_f32(O.BF16, w)) * inv[:, None]
+    for g in range(512 // group):
+        yg = y[:, g * group:(g + 1) * group]
+        want_sc = np.maximum(np.abs(yg).max(-1), np.float32(1e-12)) / np.float32(448)
+        np.testing.assert_array_equal(sc[:, g], want_sc)
+        want_q = O.f32_to_e4m3(yg * (np.float32(1) / want_sc)[:, None])
+        np.testing.assert_array_equal(q[:, g * group:(g + 1) * group], want_q)
+
+
+def test_fp8_group_power_of_two_scales():
+    x, w, r = _inputs(9, 1024, O.FP16, 8)
+    _, sc, _ = O.rms_norm_fp8_group(O.FP16, x, w, 1e-6, group=128, r=r)
+    q2, sc2, _ = O.rms_norm_fp8_group(O.FP16, x, w, 1e-6, group=128, pow2=True, r=r)
+    m, e = np.frexp(sc2)
+    assert (m == 0.5).all()  # exact powers of two
+    assert (sc2 >= sc).all() and (sc2 < 2 * sc).all()  # the smallest one not below the scale
+    # With a larger scale nothing saturates: every code is within the e4m3 range below 448.
+    mag = q2 & 0x7F
+    assert (mag != 0x7F).all() and int(mag.max()) <= 0x7E

@@ -48,3 +48,14 @@ def test_meta_kernels_trace():
     w = torch.empty(8, dtype=torch.bfloat16, device="meta")
     assert torch.ops.hp_rms_norm.rms_norm(x, w, r, 1e-6) is None
     assert torch.ops.hp_rms_norm.relu(torch.empty_like(x), x) is None
+
+
+def test_fp8_group_schema_and_meta_kernel():
+    s = str(torch.ops.hp_rms_norm.rms_norm_fp8_group.default._schema)
+    assert s == ("hp_rms_norm::rms_norm_fp8_group(Tensor(a!) out, Tensor(b!) scales, Tensor input, "
+                 "Tensor weight, Tensor(c!)? residual, float eps, int group_size, bool scale_pow2) -> ()")
+    x = torch.empty(4, 256, dtype=torch.bfloat16, device="meta")
+    w = torch.empty(256, dtype=torch.bfloat16, device="meta")
+    out = torch.empty(4, 256, dtype=torch.float8_e4m3fn, device="meta")
+    sc = torch.empty(4, 2, dtype=torch.float32, device="meta")
+    assert torch.ops.hp_rms_norm.rms_norm_fp8_group(out, sc, x, w, None, 1e-6, 128, False) is None
