@@ -575,6 +575,8 @@ VARIANTS = {
     "plain_fp8_dynamic": (False, "fp8d", 3),
     "fused_nvfp4": (True, "nvfp4", 6.5625),   # + e2m1 codes 0.5 B and a scale byte per 16
     "plain_nvfp4": (False, "nvfp4", 2.5625),
+    "fused_fp8_group128": (True, "fp8g", 7.03125),  # + one float32 scale per 128 elements
+    "plain_fp8_group128": (False, "fp8g", 3.03125),
 }
 
 
@@ -610,9 +612,16 @@ def run_variants(args, dist, dev, stream):
                         for _ in range(nsets)]
             scale = torch.tensor([0.01 if form != "nvfp4" else 336.0], device=dev)
             rsc = torch.empty(rows, device=dev)
+            gsc = torch.empty(rows, h // 128, device=dev)
             bsc = torch.empty(rows, h // 16, device=dev, dtype=torch.uint8)
 
             def call(k, sh, h=h, xs=xs, rs=rs, w=w, outs=outs, form=form, res=res):
+                if form == "fp8g":
+                    capi.rms_norm_fp8_group(outs[k].data_ptr(), gsc.data_ptr(), h // 128, 1,
+                                            xs[k].data_ptr(), w.data_ptr(),
+                                            rs[k].data_ptr() if res else None, rows, h, h, h, h,
+                                            1e-6, capi.DTYPE_BF16, 128, False, sh)
+                    return
                 if form == "nvfp4":
                     capi.rms_norm_nvfp4(outs[k].data_ptr(), bsc.data_ptr(), xs[k].data_ptr(),
                                         w.data_ptr(), rs[k].data_ptr() if res else None, rows, h,

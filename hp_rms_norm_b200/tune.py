@@ -4,7 +4,8 @@
                                     [--dtype bf16|fp16] [--warm] [--json out.json]
                                     [--no-tma | --tma-only] [--isolated] [--copy]
                                     [--variant fused|fused_out|plain|fused_fp8s|fused_fp8d|
-                                               plain_fp8s|plain_fp8d]
+                                               plain_fp8s|plain_fp8d|fused_nvfp4|plain_nvfp4|
+                                               fused_fp8g|plain_fp8g]
 
 Times every compiled launch plan that covers each requested shape (through
 ``hprn_set_plan_override``) and prints the fastest, next to the built-in
@@ -37,6 +38,8 @@ VARIANTS = {
     "plain_fp8d": (False, "fp8d", 3),
     "fused_nvfp4": (True, "nvfp4", 6.5625),
     "plain_nvfp4": (False, "nvfp4", 2.5625),
+    "fused_fp8g": (True, "fp8g", 7.03125),   # group-128 scales
+    "plain_fp8g": (False, "fp8g", 3.03125),
 }
 
 
@@ -138,7 +141,8 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
 
     res_needed, form_name, bpe = VARIANTS[variant]
     form = {"same": capi.OUT_SAME, "fp8s": capi.OUT_FP8_E4M3_STATIC,
-            "fp8d": capi.OUT_FP8_E4M3_DYNAMIC, "nvfp4": capi.OUT_NVFP4}[form_name]
+            "fp8d": capi.OUT_FP8_E4M3_DYNAMIC, "nvfp4": capi.OUT_NVFP4,
+            "fp8g": capi.OUT_FP8_E4M3_GROUP}[form_name]
 
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     code = capi.DTYPE_BF16 if dtype == "bf16" else capi.DTYPE_FP16
@@ -166,7 +170,15 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
         block_scales = torch.empty(rows, max(1, h // 16), device=dev, dtype=torch.uint8)
         byt = int(rows * h * bpe) + 2 * h + (4 * rows if form_name == "fp8d" else 0)
 
+        group_scales = torch.empty(rows, max(1, h // 128), device=dev)
+
         def run(k, s):
+            if form == capi.OUT_FP8_E4M3_GROUP:
+                capi.rms_norm_fp8_group(outs[k].data_ptr(), group_scales.data_ptr(), h // 128, 1,
+                                        xs[k].data_ptr(), w.data_ptr(),
+                                        rs[k].data_ptr() if res_needed else None, rows, h, h, h, h,
+                                        1e-6, code, 128, False, s)
+                return
             if form == capi.OUT_NVFP4:
                 capi.rms_norm_nvfp4(outs[k].data_ptr(), block_scales.data_ptr(), xs[k].data_ptr(),
                                     w.data_ptr(), rs[k].data_ptr() if res_needed else None, rows,
