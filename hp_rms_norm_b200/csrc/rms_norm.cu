@@ -92,6 +92,7 @@ struct RmsArgs {
   int64_t gs_group;
   int32_t group_vecs;
   int32_t scale_pow2;  // round group scales up to powers of two
+  int32_t lanes_per_row;  // warp kind: lanes holding one row (1..32, a power of two)
 };
 
 // Element pairs go through Blackwell's packed fp32 instructions
@@ -262,6 +263,18 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Butterflies over aligned groups of `width` lanes (a power of two, 1..32):
+// every lane ends with its group's result; width 32 is warp_sum / warp_max.
+__device__ __forceinline__ float lane_group_sum(float v, int width) {
+  for (int o = width >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float lane_group_max(float v, int width) {
+  for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -379,16 +392,20 @@ __device__ __forceinline__ void store_group_fp8(const RmsArgs& a, int64_t row, i
 }
 
 // ---------------------------------------------------------------------------
-// Kernel 1: one warp per row (rows of at most 4 * 32 vectors).  No shared
-// memory, no block barrier: a warp that has finished its row retires without
-// waiting for the rest of its CTA.
+// Kernel 1: rows of at most 4 * 32 vectors, each held by `lanes_per_row`
+// lanes of one warp (a whole warp, or 32 / lanes_per_row rows per warp for
+// short rows: 1-32 lanes, a power of two), reduced by a butterfly over those
+// lanes.  No shared memory, no block barrier.  Lanes past the last row stay
+// in the warp (their loads and stores are skipped) so every shuffle has all
+// 32 lanes.
 template <typename T, int VEC, int VPT, bool RES, int OUT>
 __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + (threadIdx.x >> 5);
+  const int lpr = a.lanes_per_row;
+  const int sub = threadIdx.x & (lpr - 1);
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + threadIdx.x / lpr;
+  const bool active = row < a.rows;
   pdl_entry();
-  if (row >= a.rows) return;
   const uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
   const uint64_t pol_stream = policy_evict_first();
@@ -397,8 +414,8 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   Vec<VEC> xv[VPT], rv[VPT], wv[VPT];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int v = lane + 32 * j;
-    if (v < a.nvec) {
+    const int v = sub + lpr * j;
+    if (active && v < a.nvec) {
       xv[j] = ld_stream<VEC>(xr + v * EPV, pol_stream);
       if constexpr (RES) rv[j] = ld_stream<VEC>(rr + v * EPV, pol_stream);
     }
@@ -410,8 +427,8 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   float m = 0.f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int v = lane + 32 * j;
-    if (v < a.nvec) {
+    const int v = sub + lpr * j;
+    if (active && v < a.nvec) {
       if constexpr (RES) {
         add_round<T, VEC>(xv[j], rv[j], a0, a1);
         st_global<VEC>(rr + v * EPV, xv[j]);
@@ -426,23 +443,24 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   if constexpr (RES && OUT == kOutFp8Dynamic) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int v = lane + 32 * j;
-      if (v < a.nvec) m = vec_amax_rw<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), m);
+      const int v = sub + lpr * j;
+      if (active && v < a.nvec)
+        m = vec_amax_rw<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), m);
     }
   }
-  const float inv = rsqrtf(fmaf(warp_sum(a0 + a1), a.inv_hidden, a.eps));
+  const float inv = rsqrtf(fmaf(lane_group_sum(a0 + a1, lpr), a.inv_hidden, a.eps));
   float inv_scale = static_inv_scale<OUT>(a);
   if constexpr (OUT == kOutFp8Dynamic) {
-    const float scale = fmaxf(warp_max(m) * inv, kMinAmax) / kE4m3Max;
+    const float scale = fmaxf(lane_group_max(m, lpr) * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
-    if (lane == 0) a.row_scales[row] = scale;
+    if (sub == 0 && active) a.row_scales[row] = scale;
   }
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
-    const int v = lane + 32 * j;
+    const int v = sub + lpr * j;
     if constexpr (OUT == kOutFp8Group) {
-      store_group_fp8<T, VEC, RES>(a, row, v, v < a.nvec, xv[j], wv[j], inv, pol_keep);
-    } else if (v < a.nvec) {
+      store_group_fp8<T, VEC, RES>(a, row, v, active && v < a.nvec, xv[j], wv[j], inv, pol_keep);
+    } else if (active && v < a.nvec) {
       store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
                              inv_scale);
     }
@@ -889,7 +907,8 @@ int slice_vecs_of(int nvec, int cluster, int out) {
 //   * one CTA per row with as many threads as the row has 32-byte vectors
 //     (one vector per thread): the most warps per SM, so the most loads in
 //     flight, and the shortest serial chain per thread;
-//   * rows of at most 64 vectors: one warp per row, eight rows per CTA;
+//   * rows of at most 16 vectors: one vector per lane, several rows per
+//     warp; rows of 17..64 vectors: one warp per row, eight rows per CTA;
 //   * rows of 1025..2048 vectors: two vectors per thread (four below ~1440
 //     vectors, where 1024-thread CTAs would leave SMs a CTA short);
 //   * thread-block clusters only once a row no longer fits one CTA: splitting
@@ -919,6 +938,21 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
   const int ext = nvec <= 2048 ? extended_vpt(nvec, residual, out) : -1;
   if (nvec <= 64 || ext == 0) {
     p.kind = kWarpRows;
+    if (nvec <= 16) {
+      // Short rows (hidden <= 256 at 32-byte vectors, e.g. per-head norms):
+      // one vector per lane, 32 / lanes rows per warp, 256-thread CTAs.  At
+      // 131072 rows x hidden 64-256: 3.2-4.3x one warp per row, as fast as
+      // torch's copy of the same bytes.
+      int lanes = 1;
+      while (lanes < nvec) lanes <<= 1;
+      // Per-group fp8: eight lanes (a group's lanes must share one row), one
+      // or two vectors each (hidden 256: 25.3 vs 28.1 us with sixteen lanes).
+      if (out == kOutFp8Group) lanes = 8;
+      p.vpt = (nvec + lanes - 1) / lanes;
+      p.tpr = lanes;
+      p.rows_per_cta = 256 / lanes;
+      return p;
+    }
     p.vpt = nvec <= 64 ? (nvec + 31) / 32 : 4;
     p.tpr = 32;
     // Eight warp-rows (256 threads) per CTA: best or level for every form at
@@ -1050,12 +1084,19 @@ bool plan_valid(const Plan& p, int nvec, int max_vec, const Variant& var, std::s
     return false;
   }
   switch (p.kind) {
-    case kWarpRows:
-      if (p.tpr != 32 || p.rows_per_cta < 1 || p.rows_per_cta > 8 || p.vpt * 32 < nvec) {
-        *why = "warp plan needs tpr 32, 1..8 rows per CTA and vpt*32 >= vectors per row";
+    case kWarpRows: {
+      // tpr = lanes per row (a power of two); rows_per_cta rows of tpr lanes
+      // fill whole warps of a CTA of at most 256 threads.
+      const bool pow2 = p.tpr >= 1 && p.tpr <= 32 && (p.tpr & (p.tpr - 1)) == 0;
+      const int threads = p.rows_per_cta * p.tpr;
+      if (!pow2 || p.rows_per_cta < 1 || threads % 32 || threads > 256 || p.vpt * p.tpr < nvec ||
+          (var.out == kOutFp8Group && p.tpr < 8)) {
+        *why = "warp plan needs tpr (lanes per row) a power of two <= 32 (>= 8 for per-group "
+               "fp8), rpc * tpr a multiple of 32 up to 256, and vpt * tpr >= vectors per row";
         return false;
       }
       return true;
+    }
     case kCtaRows:
     case kClusterRows: {
       const int c = p.kind == kCtaRows ? 1 : p.cluster;
@@ -1403,6 +1444,7 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   a.gs_group = q.gs_group;
   a.group_vecs = q.out_form == kOutFp8Group ? q.group_size / epv : 1;
   a.scale_pow2 = q.scale_pow2 != 0;
+  a.lanes_per_row = p.kind == kWarpRows ? p.tpr : 32;
   *plan = p;
   *args = a;
   return HPRN_OK;
@@ -1474,7 +1516,7 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
   if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
   if (p.kind == kTma) return launch_tma(p, a, fn, dev, stream, flags);
   // Rows handled per CTA-group in grid.x; split very tall problems into launches.
-  const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;
+  const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;  // rows per CTA
   const bool clustered = p.kind == kClusterRows || (p.kind == kTwoPass && p.cluster > 1);
   const int64_t ctas_per_unit = clustered ? p.cluster : 1;
   const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
@@ -1496,7 +1538,7 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(static_cast<unsigned>(units * ctas_per_unit), 1, 1);
-    cfg.blockDim = dim3(p.kind == kWarpRows ? 32 * p.rows_per_cta : p.tpr, 1, 1);
+    cfg.blockDim = dim3(p.kind == kWarpRows ? p.rows_per_cta * p.tpr : p.tpr, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cfg.attrs = attr;

@@ -77,6 +77,11 @@ def candidates(nvec: int, full: bool = True) -> list[str]:
     if nvec <= 128:
         vpt = min(v for v in warp_vpts if v * 32 >= nvec)
         out += [f"warp:vec32:vpt{vpt}:tpr32:cluster1:rpc{r}" for r in (2, 4, 8)]
+    if nvec <= 64:  # several short rows per warp: tpr lanes per row
+        for lanes in (1, 2, 4, 8, 16):
+            vpt = -(-nvec // lanes)
+            if vpt in warp_vpts:
+                out += [f"warp:vec32:vpt{vpt}:tpr{lanes}:cluster1:rpc{t // lanes}" for t in (128, 256)]
     for cl in (1, 2, 4, 8):
         for vpt in cta_vpts:
             if cl > 1 and not full and vpt == 1:

@@ -68,6 +68,11 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     (131072, "cluster:vec32:vpt2:tpr512:cluster8:rpc1"),
     (262144, "cluster:vec32:vpt2:tpr1024:cluster8:rpc1"),
     (262160, "twopass:vec32:vpt4:tpr256:cluster8:rpc1"),
+    # short rows: several rows per warp, one vector per lane
+    (16, "warp:vec32:vpt1:tpr1:cluster1:rpc256"),
+    (64, "warp:vec32:vpt1:tpr4:cluster1:rpc64"),
+    (256, "warp:vec32:vpt1:tpr16:cluster1:rpc16"),
+    (512, "warp:vec32:vpt1:tpr32:cluster1:rpc8"),
     # the config-1 sweep's regimes
     (20480, "cta:vec32:vpt4:tpr320:cluster1:rpc1"),
     (24576, "cta:vec32:vpt2:tpr768:cluster1:rpc1"),
@@ -113,7 +118,7 @@ def test_plan_covers_every_row_length():
         nvec = hidden // (vec // 2)
         assert hidden % (vec // 2) == 0, (hidden, p)
         if p.startswith("warp"):
-            assert vpt * 32 >= nvec, (hidden, p)
+            assert vpt * tpr >= nvec, (hidden, p)
         elif not p.startswith("twopass"):
             assert tpr * vpt * cl >= nvec, (hidden, p)
 

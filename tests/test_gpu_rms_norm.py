@@ -145,6 +145,13 @@ FORCED = [
     (9, 4097, "twopass:vec2:vpt4:tpr512:cluster4:rpc1"),
     (33, 256, "warp:vec16:vpt1:tpr32:cluster1:rpc8"),
     (33, 256, "warp:vec4:vpt4:tpr32:cluster1:rpc3"),
+    (67, 64, "warp:vec32:vpt1:tpr4:cluster1:rpc64"),
+    (5, 128, "warp:vec32:vpt2:tpr4:cluster1:rpc32"),
+    (129, 256, "warp:vec32:vpt1:tpr16:cluster1:rpc16"),
+    (33, 48, "warp:vec32:vpt3:tpr1:cluster1:rpc128"),
+    (17, 512, "warp:vec32:vpt4:tpr8:cluster1:rpc32"),
+    (9, 40, "warp:vec16:vpt2:tpr4:cluster1:rpc8"),
+    (300, 16, "warp:vec32:vpt1:tpr1:cluster1:rpc256"),
 ]
 
 

@@ -88,6 +88,9 @@ FORCED = [
     (64, 1024, "warp:vec32:vpt2:tpr32:cluster1:rpc4"),
     (33, 512, "warp:vec32:vpt1:tpr32:cluster1:rpc8"),
     (17, 2048, "warp:vec32:vpt4:tpr32:cluster1:rpc1"),
+    (67, 64, "warp:vec32:vpt1:tpr4:cluster1:rpc64"),
+    (37, 256, "warp:vec32:vpt2:tpr8:cluster1:rpc32"),
+    (11, 128, "warp:vec32:vpt4:tpr2:cluster1:rpc64"),
     (9, 4096, "cta:vec32:vpt2:tpr128:cluster1:rpc1"),
     (9, 8192, "cta:vec32:vpt4:tpr128:cluster1:rpc1"),
     (9, 8192, "cta:vec16:vpt4:tpr256:cluster1:rpc1"),
