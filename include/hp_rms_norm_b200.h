@@ -220,8 +220,9 @@ HPRN_API int hprn_version(void);
  * hprn_rms_norm would use for this problem on the current device into
  * `plan` as a NUL-terminated string "<kind>:vec<V>:vpt<P>:tpr<T>:cluster<C>:rpc<R>"
  * (kind warp | cta | cluster | twopass | tma; V bytes per vector access; P
- * vectors per thread; T threads per CTA; C CTAs per row; R rows per CTA, or for
- * kind tma the depth of the CTA's ring of TMA-staged rows) and returns HPRN_OK.  Performs no launch.  Null input/residual pointers plan for
+ * vectors per thread; T threads per CTA, or for kind warp the lanes holding one
+ * row (1..32, a power of two); C CTAs per row; R rows per CTA, or for kind tma
+ * the depth of the CTA's ring of TMA-staged rows) and returns HPRN_OK.  Performs no launch.  Null input/residual pointers plan for
  * 256-byte-aligned tensors; without a usable device it plans for a 148-SM B200.
  */
 HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* input,
