@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(256) act_and_mul_rows(ActArgs a) {
   uint16_t* dst = a.out + row * a.out_stride;
   const uint64_t pol = policy_evict_first();
   const int64_t base = chunk * (static_cast<int64_t>(blockDim.x) * U) + threadIdx.x;
-  pdl_entry();
+  pdl_wait();
 
   Vec<VEC> g[U], u[U];
 #pragma unroll
@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(256) act_and_mul_rows(ActArgs a) {
     const int64_t i = base + static_cast<int64_t>(k) * blockDim.x;
     if (i < a.nvec) st_global<VEC>(dst + i * EPV, act_mul<T, VEC, ACT>(g[k], u[k]));
   }
+  pdl_trigger();
 }
 
 using ActFn = void (*)(ActArgs);

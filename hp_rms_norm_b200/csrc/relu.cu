@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(256) relu_rows(ReluArgs a) {
   uint16_t* dst = a.out + row * a.out_stride;
   const uint64_t pol = policy_evict_first();
   const int64_t base = chunk * (static_cast<int64_t>(blockDim.x) * U) + threadIdx.x;
-  pdl_entry();
+  pdl_wait();
 
   Vec<VEC> v[U];
 #pragma unroll
@@ -93,6 +93,7 @@ __global__ void __launch_bounds__(256) relu_rows(ReluArgs a) {
       dst[e] = relu_vec<T, 2>(s).h;
     }
   }
+  pdl_trigger();
 }
 
 using ReluFn = void (*)(ReluArgs);

@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   const int sub = threadIdx.x & (lpr - 1);
   const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + threadIdx.x / lpr;
   const bool active = row < a.rows;
-  pdl_entry();
+  pdl_wait();
   const uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
   const uint64_t pol_stream = policy_evict_first();
@@ -465,6 +465,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
                              inv_scale);
     }
   }
+  pdl_trigger();
 }
 
 // Largest CTA a cta/cluster kernel with VPT vectors per thread is compiled
@@ -497,7 +498,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   int64_t row;
   int v_begin = 0, v_end = a.nvec;
   uint32_t crank = 0, csize = 1;
-  pdl_entry();
+  pdl_wait();
   if constexpr (CLUSTER) {
     // Phase 1 of the cluster barrier: completes once every CTA of the cluster
     // is running, which makes their shared memory safe to write.
@@ -591,6 +592,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
                              inv_scale);
     }
   }
+  pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------
@@ -617,7 +619,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   int64_t row;
   int v_begin = 0, v_end = a.nvec;
   uint32_t crank = 0, csize = 1;
-  pdl_entry();
+  pdl_wait();
   if constexpr (CLUSTER) {
     cluster_arrive_relaxed();  // phase 1: completes once every peer is running
     crank = cluster_ctarank();
@@ -691,6 +693,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
       }
     }
   }
+  pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------
@@ -757,7 +760,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_
     if constexpr (RES) bulk_load(dst + row_bytes, a.r + row * a.r_stride, row_bytes, bar, pol_stream);
   };
 
-  pdl_entry();
+  pdl_wait();
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) mbar_init(smem_u32(&full[s]), 1);
     mbar_init_fence();
@@ -826,6 +829,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_
     }
     if (++s == stages) s = 0, parity ^= 1u;
   }
+  pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------

@@ -46,8 +46,9 @@ typedef enum hprn_dtype {
  *   dependent launch).  The kernel may then be scheduled while the previous
  *   kernel on the stream is still finishing; it waits (griddepcontrol.wait)
  *   for that kernel to complete before its first memory access, so results
- *   are the same as a plain launch.  Every kernel of this library also allows
- *   its own successor to start early in the same way.
+ *   are the same as a plain launch.  Every kernel of this library also lets
+ *   its own successor be scheduled early, once all of its CTAs have issued
+ *   their last store.
  */
 #define HPRN_LAUNCH_PDL 1u
 #define HPRN_LAUNCH_DEFAULT HPRN_LAUNCH_PDL

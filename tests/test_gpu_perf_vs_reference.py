@@ -138,9 +138,18 @@ def test_decode_not_slower_than_reference_kernel(cuda, ref_kernels, rows, hidden
         ref_kernels.rms_norm(x, w, r, 1e-5, s)
 
     t_ours, t_ref = graph_us(ours, 1), graph_us(ref, 1)
-    _decode[f"{str(dtype)[6:]} {rows}x{hidden}"] = {"ours_us": round(t_ours, 2),
-                                                    "ref_us": round(t_ref, 2),
-                                                    "speedup": round(t_ref / t_ours, 3)}
+    key = f"{str(dtype)[6:]} {rows}x{hidden}"
+    _decode[key] = {"ours_us": round(t_ours, 2), "ref_us": round(t_ref, 2),
+                    "speedup": round(t_ref / t_ours, 3)}
+    fi = flashinfer_fused_add_rmsnorm()
+    if fi is not None:  # library comparator: recorded, not asserted
+        def flashinfer(k, s):
+            with torch.cuda.stream(torch.cuda.ExternalStream(s)):
+                fi(x, r, w, eps=1e-5)
+
+        t_fi = graph_us(flashinfer, 1)
+        _decode[key]["flashinfer_us"] = round(t_fi, 2)
+        _decode[key]["speedup_vs_flashinfer"] = round(t_fi / t_ours, 3)
     out = os.environ.get("HPRN_PERF_JSON")
     if out:
         with open(out.replace(".json", "_decode.json"), "w") as f:
