@@ -93,6 +93,17 @@ def candidates(nvec: int, full: bool = True) -> list[str]:
                 continue
             kind = "cta" if cl == 1 else "cluster"
             out.append(f"{kind}:vec32:vpt{vpt}:tpr{tpr}:cluster{cl}:rpc1")
+    # 16-byte vectors (twice the threads for the same row) for rows that fit
+    # one CTA: more, smaller accesses in flight per row.
+    n16 = 2 * nvec
+    for vpt in (1, 2):
+        tpr = -(-(-(-n16 // vpt)) // 32) * 32
+        if 32 <= tpr <= 1024:
+            out.append(f"cta:vec16:vpt{vpt}:tpr{tpr}:cluster1:rpc1")
+    if n16 <= 128:
+        vpt16 = -(-n16 // 32)
+        if vpt16 in warp_vpts:
+            out += [f"warp:vec16:vpt{vpt16}:tpr32:cluster1:rpc{r}" for r in (4, 8)]
     if nvec > 8 * 2048:  # two passes, one CTA or a cluster per row
         out += [f"twopass:vec32:vpt4:tpr{t}:cluster{cl}:rpc1" for cl in (1, 2, 4, 8) for t in (256, 512)]
     return out
