@@ -28,7 +28,7 @@ BUILD = os.path.join(ROOT, "_build")
 LIB_NAME = "libhp_rms_norm_b200.so"
 LIB = os.path.join(PKG, LIB_NAME)
 CUDA_SOURCES = ["rms_norm.cu", "relu.cu", "act_and_mul.cu", "runtime.cu"]
-HEADERS = ["vec.cuh", "bulk.cuh", "runtime.cuh"]
+HEADERS = ["vec.cuh", "bulk.cuh", "runtime.cuh", "rms_norm_kernels.cuh"]
 
 # HPRN_DEBUG=1 (or the reference's own DEBUG=1, setup.py:23-28 there) builds
 # host code without optimisation and with debug symbols (device code keeps -O3
