@@ -143,10 +143,21 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
     }
     p.vpt = nvec <= 64 ? (nvec + 31) / 32 : 4;
     p.tpr = 32;
-    // Eight warp-rows (256 threads) per CTA: best or level for every form at
-    // hidden 1024-2048 (fused 6.60 vs 7.13 us with two at 4096 x 1024; plain
-    // 7.03 vs 7.57 us with four at 4096 x 2048).
-    p.rows_per_cta = 8;
+    // Four warp-rows (128 threads) per CTA: best or within 2% for every form
+    // at hidden 1024-2048 with the programmatic-launch trigger at each
+    // kernel's end (fused 6.52-6.55 vs 6.70-6.79 us with eight at 4096 x
+    // 1024); plain 16-bit rows of <= 64 vectors keep eight (4.36 vs 4.50 us).
+    p.rows_per_cta = (!residual && out == kOutSame && nvec <= 64) ? 8 : 4;
+    return p;
+  }
+  if (residual && out == kOutSame && nvec <= 96) {
+    // Fused rows of 65..96 vectors (hidden 1040-1536): one warp per row at
+    // three vectors per lane beat one CTA per row (9.00 vs 9.38 us at 4096 x
+    // 1536).
+    p.kind = kWarpRows;
+    p.vpt = 3;
+    p.tpr = 32;
+    p.rows_per_cta = 4;
     return p;
   }
   if (!residual && out == kOutNvfp4 && nvec > 1536 && nvec <= 2048) {

@@ -56,7 +56,8 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     assert capi.plan(4096, 16384) == capi.plan(4096, 16384, input_ptr=1 << 20,
                                                residual_ptr=1 << 21)
     assert capi.plan(4096, 16384) == "cta:vec32:vpt1:tpr1024:cluster1:rpc1"
-    assert capi.plan(4096, 1024) == "warp:vec32:vpt2:tpr32:cluster1:rpc8"
+    assert capi.plan(4096, 1024) == "warp:vec32:vpt2:tpr32:cluster1:rpc4"
+    assert capi.plan(4096, 1536) == "warp:vec32:vpt3:tpr32:cluster1:rpc4"
 
 
 @pytest.mark.parametrize("hidden,plan", [
@@ -72,7 +73,7 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     (16, "warp:vec32:vpt1:tpr1:cluster1:rpc256"),
     (64, "warp:vec32:vpt1:tpr4:cluster1:rpc64"),
     (256, "warp:vec32:vpt1:tpr16:cluster1:rpc16"),
-    (512, "warp:vec32:vpt1:tpr32:cluster1:rpc8"),
+    (512, "warp:vec32:vpt1:tpr32:cluster1:rpc4"),
     # the config-1 sweep's regimes
     (20480, "cta:vec32:vpt4:tpr320:cluster1:rpc1"),
     (24576, "cta:vec32:vpt2:tpr768:cluster1:rpc1"),
