@@ -187,3 +187,54 @@ def test_relu_against_reference_activation_kernel(cuda, ref_kernels, shape, dtyp
         with open(out.replace(".json", "_decode.json"), "w") as f:
             json.dump(_decode, f, indent=1)
     assert byt / t_ours / 1e3 >= 0.85 * 6532.9
+
+
+_ext = {}
+
+
+@pytest.mark.parametrize("form,rows,hidden", [
+    ("plain", 4096, 2048), ("plain", 4096, 4096), ("plain", 4096, 8192), ("plain", 4096, 16384),
+    ("plain", 131072, 128), ("fused_fp8_static", 4096, 2048), ("fused_fp8_static", 4096, 4096),
+    ("fused_fp8_static", 4096, 8192), ("fused_fp8_static", 4096, 16384)])
+def test_extended_forms_vs_flashinfer(cuda, form, rows, hidden):
+    """Plain RMSNorm and fused add + RMSNorm with a static-scale fp8 output,
+    next to FlashInfer's rmsnorm / fused_add_rmsnorm_quant (library
+    comparators, timed the same way: cold rotating buffers; recorded, not
+    asserted)."""
+    try:
+        from flashinfer.norm import fused_add_rmsnorm_quant, rmsnorm
+    except Exception:
+        pytest.skip("FlashInfer not installed")
+    nsets = max(2, -(-600_000_000 // (rows * hidden * 4)))
+    xs = [torch.randn(rows, hidden, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
+    rs = [torch.randn(rows, hidden, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
+    w = (1 + 0.1 * torch.randn(hidden, device=cuda)).to(torch.bfloat16)
+    fp8 = form == "fused_fp8_static"
+    outs = [torch.empty(rows, hidden, device=cuda, dtype=torch.float8_e4m3fn if fp8 else torch.bfloat16)
+            for _ in range(nsets)]
+    scale = torch.tensor([0.02], device=cuda)
+
+    def ours(k, s):
+        capi.rms_norm_out(outs[k].data_ptr(), xs[k].data_ptr(), w.data_ptr(),
+                          rs[k].data_ptr() if fp8 else None, rows, hidden, hidden, hidden, hidden,
+                          1e-6, capi.DTYPE_BF16,
+                          capi.OUT_FP8_E4M3_STATIC if fp8 else capi.OUT_SAME, scale.data_ptr(),
+                          None, s)
+
+    def theirs(k, s):
+        with torch.cuda.stream(torch.cuda.ExternalStream(s)):
+            if fp8:
+                fused_add_rmsnorm_quant(outs[k], xs[k], rs[k], w, scale, eps=1e-6)
+            else:
+                rmsnorm(xs[k], w, eps=1e-6, out=outs[k])
+
+    t_ours = graph_us(ours, nsets)
+    t_fi = graph_us(theirs, nsets)
+    byt = rows * hidden * (7 if fp8 else 4) + 2 * hidden
+    _ext[f"{form} {rows}x{hidden}"] = {"ours_us": round(t_ours, 2), "flashinfer_us": round(t_fi, 2),
+                                       "speedup_vs_flashinfer": round(t_fi / t_ours, 3),
+                                       "ours_gbs": round(byt / t_ours / 1e3, 1)}
+    out = os.environ.get("HPRN_PERF_JSON")
+    if out:
+        with open(out.replace(".json", "_ext.json"), "w") as f:
+            json.dump(_ext, f, indent=1)
