@@ -195,16 +195,19 @@ _ext = {}
 @pytest.mark.parametrize("form,rows,hidden", [
     ("plain", 4096, 2048), ("plain", 4096, 4096), ("plain", 4096, 8192), ("plain", 4096, 16384),
     ("plain", 131072, 128), ("fused_fp8_static", 4096, 2048), ("fused_fp8_static", 4096, 4096),
-    ("fused_fp8_static", 4096, 8192), ("fused_fp8_static", 4096, 16384)])
+    ("fused_fp8_static", 4096, 8192), ("fused_fp8_static", 4096, 16384),
+    ("fused_nvfp4", 4096, 4096), ("fused_nvfp4", 4096, 8192), ("fused_nvfp4", 4096, 16384)])
 def test_extended_forms_vs_flashinfer(cuda, form, rows, hidden):
-    """Plain RMSNorm and fused add + RMSNorm with a static-scale fp8 output,
-    next to FlashInfer's rmsnorm / fused_add_rmsnorm_quant (library
-    comparators, timed the same way: cold rotating buffers; recorded, not
-    asserted)."""
+    """Plain RMSNorm, fused add + RMSNorm with a static-scale fp8 output, and
+    fused add + RMSNorm with an NVFP4 output, next to FlashInfer's rmsnorm /
+    fused_add_rmsnorm_quant / add_rmsnorm_fp4quant (library comparators, timed
+    the same way: cold rotating buffers; recorded, not asserted)."""
     try:
-        from flashinfer.norm import fused_add_rmsnorm_quant, rmsnorm
+        from flashinfer.norm import add_rmsnorm_fp4quant, fused_add_rmsnorm_quant, rmsnorm
     except Exception:
         pytest.skip("FlashInfer not installed")
+    if form == "fused_nvfp4":
+        return _nvfp4_vs_flashinfer(cuda, rows, hidden, add_rmsnorm_fp4quant)
     nsets = max(2, -(-600_000_000 // (rows * hidden * 4)))
     xs = [torch.randn(rows, hidden, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
     rs = [torch.randn(rows, hidden, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
@@ -234,6 +237,37 @@ def test_extended_forms_vs_flashinfer(cuda, form, rows, hidden):
     _ext[f"{form} {rows}x{hidden}"] = {"ours_us": round(t_ours, 2), "flashinfer_us": round(t_fi, 2),
                                        "speedup_vs_flashinfer": round(t_fi / t_ours, 3),
                                        "ours_gbs": round(byt / t_ours / 1e3, 1)}
+    out = os.environ.get("HPRN_PERF_JSON")
+    if out:
+        with open(out.replace(".json", "_ext.json"), "w") as f:
+            json.dump(_ext, f, indent=1)
+
+
+def _nvfp4_vs_flashinfer(cuda, rows, hidden, add_rmsnorm_fp4quant):
+    nsets = max(2, -(-600_000_000 // (rows * hidden * 4)))
+    xs = [torch.randn(rows, hidden, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
+    rs = [torch.randn(rows, hidden, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
+    w = (1 + 0.1 * torch.randn(hidden, device=cuda)).to(torch.bfloat16)
+    gs = torch.tensor([336.0], device=cuda)
+    codes = [torch.empty(rows, hidden // 2, device=cuda, dtype=torch.uint8) for _ in range(nsets)]
+    sf = torch.empty(rows, hidden // 16, device=cuda, dtype=torch.uint8)
+
+    def ours(k, s):
+        capi.rms_norm_nvfp4(codes[k].data_ptr(), sf.data_ptr(), xs[k].data_ptr(), w.data_ptr(),
+                            rs[k].data_ptr(), rows, hidden, hidden, hidden, hidden, 1e-6,
+                            capi.DTYPE_BF16, gs.data_ptr(), s)
+
+    def theirs(k, s):
+        with torch.cuda.stream(torch.cuda.ExternalStream(s)):
+            add_rmsnorm_fp4quant(xs[k], rs[k], w, global_scale=gs, eps=1e-6)
+
+    t_ours = graph_us(ours, nsets)
+    t_fi = graph_us(theirs, nsets)
+    byt = int(rows * hidden * 6.5625) + 2 * hidden
+    _ext[f"fused_nvfp4 {rows}x{hidden}"] = {"ours_us": round(t_ours, 2),
+                                           "flashinfer_us": round(t_fi, 2),
+                                           "speedup_vs_flashinfer": round(t_fi / t_ours, 3),
+                                           "ours_gbs": round(byt / t_ours / 1e3, 1)}
     out = os.environ.get("HPRN_PERF_JSON")
     if out:
         with open(out.replace(".json", "_ext.json"), "w") as f:
