@@ -272,3 +272,38 @@ def _nvfp4_vs_flashinfer(cuda, rows, hidden, add_rmsnorm_fp4quant):
     if out:
         with open(out.replace(".json", "_ext.json"), "w") as f:
             json.dump(_ext, f, indent=1)
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu", "gelu_tanh"])
+def test_gated_activations_vs_flashinfer(cuda, act):
+    """act(gate) * up on [4096, 2 x 14336] bf16, next to FlashInfer's
+    {silu,gelu,gelu_tanh}_and_mul (library comparator, timed the same way;
+    recorded, not asserted)."""
+    try:
+        import flashinfer.activation as fa
+    except Exception:
+        pytest.skip("FlashInfer not installed")
+    rows, d = 4096, 14336
+    nsets = max(2, -(-600_000_000 // (rows * d * 6)))
+    xs = [torch.randn(rows, 2 * d, device=cuda).to(torch.bfloat16) for _ in range(nsets)]
+    outs = [torch.empty(rows, d, device=cuda, dtype=torch.bfloat16) for _ in range(nsets)]
+    code = {"silu": capi.ACT_SILU, "gelu": capi.ACT_GELU, "gelu_tanh": capi.ACT_GELU_TANH}[act]
+    fi = getattr(fa, f"{act}_and_mul")
+
+    def ours(k, s):
+        capi.act_and_mul(outs[k].data_ptr(), xs[k].data_ptr(), rows, d, d, 2 * d, code,
+                         capi.DTYPE_BF16, s)
+
+    def theirs(k, s):
+        with torch.cuda.stream(torch.cuda.ExternalStream(s)):
+            fi(xs[k], out=outs[k])
+
+    t_ours = graph_us(ours, nsets)
+    t_fi = graph_us(theirs, nsets)
+    _ext[f"{act}_and_mul {rows}x{d}"] = {"ours_us": round(t_ours, 2), "flashinfer_us": round(t_fi, 2),
+                                        "speedup_vs_flashinfer": round(t_fi / t_ours, 3),
+                                        "ours_gbs": round(rows * d * 6 / t_ours / 1e3, 1)}
+    out = os.environ.get("HPRN_PERF_JSON")
+    if out:
+        with open(out.replace(".json", "_ext.json"), "w") as f:
+            json.dump(_ext, f, indent=1)
