@@ -304,6 +304,41 @@ def test_matches_reference_cuda_kernel(cuda, hidden):
     assert int(ulp_distance(x, xr).max()) <= 1
 
 
+@pytest.mark.skipif(not os.path.exists(REF_SO), reason="reference kernels not built (oracle/_ref)")
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_reference_test_grid_matches_reference_cuda_kernel(cuda, dtype):
+    """The reference test's own grid (hidden 128..32768 in steps of 128, a
+    random token count of 1..4096 per shape, inputs and weight ~ N(0, 0.1),
+    eps = bf16 epsilon; test/test_hp_rms_norm.py:49-58), seeded, up to hidden
+    24448 (the reference's build on this toolchain rejects >= 24576), through
+    the reference's own CUDA kernel and this library: residual bit-exact,
+    output within 1 ulp at every shape."""
+    tdtype, _ = DTYPES[dtype]
+    ref = O.ReferenceKernels(REF_SO)
+    rng = np.random.default_rng(2024 if dtype == "bf16" else 2025)
+    worst, differing, total = 0, 0, 0
+    for hidden in range(128, 24448 + 1, 128):
+        rows = int(rng.integers(1, 4097))
+        g = torch.Generator(device=cuda).manual_seed(hidden)  # the "rt" distribution, on the device
+        x = (0.1 * torch.randn(rows, hidden, generator=g, device=cuda)).to(tdtype)
+        r = (0.1 * torch.randn(rows, hidden, generator=g, device=cuda)).to(tdtype)
+        w = (0.1 * torch.randn(hidden, generator=g, device=cuda)).to(tdtype)
+        eps = float(torch.finfo(torch.bfloat16).eps)
+        xr, rr = x.clone(), r.clone()
+        ref.rms_norm(xr, w, rr, eps)
+        run_capi(x, w, r, eps)
+        assert torch.equal(r.view(torch.int16), rr.view(torch.int16)), f"residual differs at {rows}x{hidden}"
+        d = ulp_distance(x, xr)
+        m = int(d.max())
+        assert m <= 1, f"output {m} ulp from the reference kernel at {rows}x{hidden}"
+        worst = max(worst, m)
+        differing += int((d > 0).sum())
+        total += d.numel()
+    # Outputs that differ by one ulp come from the sum of squares' order
+    # (a different reduction tree); they stay rare.
+    assert differing / total < 0.01, differing / total
+
+
 @pytest.mark.parametrize("hidden", [1024, 4096, 20480, 65536])
 def test_pdl_chains_match_plain_launches(cuda, hidden):
     """Back-to-back dependent launches (each call reads the previous call's
