@@ -120,7 +120,7 @@ int extended_vpt(int nvec, bool residual, int out) {
 
 // Every plan default_plan returns is compiled for the variant it is returned
 // for; two passes (rows past 8 * 2048 vectors) exist for 16-bit outputs only.
-Plan default_plan(int nvec, int vec, bool residual, int out) {
+Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
   Plan p;
   p.vec = vec;
   const int ext = nvec <= 2048 ? extended_vpt(nvec, residual, out) : -1;
@@ -191,6 +191,29 @@ Plan default_plan(int nvec, int vec, bool residual, int out) {
   // vector per thread up to 512 vectors per CTA, else two (hidden 40960-131072
   // at batch 4096: 0.88-0.95 of the copy peak, against 0.76-0.86 for the
   // smallest cluster that fits).
+  const int64_t elems = static_cast<int64_t>(nvec) * (vec / 2);
+  const bool many_rows = rows >= 1024 && vec >= 16;
+  if (residual && out == kOutSame && nvec > 4096 && (elems > 98304 || (elems > 65536 && many_rows))) {
+    // Fused 16-bit rows past 65536 elements (past 98304 for small batches):
+    // two passes, the second re-reading the row's residual from L2, beat
+    // every register-resident cluster plan, reaching 1.00-1.03 of the copy
+    // peak at hidden 81920-262144 x 4096 rows (1.15-1.38x the clustered
+    // kernel).  Up to 98304 elements with enough rows to fill the GPU, one
+    // 512-thread CTA per row; else an eight-CTA cluster per row, 128 threads
+    // per CTA up to 262144 elements and 256 past it (64-1024 rows x hidden
+    // 512K-1M).  At 64 rows x 81920 the register-resident cluster stays 13%
+    // faster, hence the larger threshold for small batches.
+    p.kind = kTwoPass;
+    p.vpt = 4;
+    if (elems <= 98304 && many_rows) {
+      p.cluster = 1;
+      p.tpr = 512;
+    } else {
+      p.cluster = 8;
+      p.tpr = elems <= 262144 ? 128 : 256;
+    }
+    return p;
+  }
   if (residual && out == kOutSame && nvec <= 8 * 2048) {
     const int slice = (nvec + 7) / 8;
     p.kind = kClusterRows;
@@ -607,7 +630,7 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
                 "fp8 output needs hidden_dim % 4 == 0 and 8-byte aligned input/weight/residual "
                 "rows and 4-byte aligned output rows");
   const int nvec = static_cast<int>(q.hidden / (max_vec / 2));
-  Plan p = default_plan(nvec, max_vec, var.res, var.out);
+  Plan p = default_plan(nvec, max_vec, var.res, var.out, q.rows);
   if (p.kind == kTwoPass && q.out_form != kOutSame)
     return fail(HPRN_ERR_INVALID_ARGUMENT, "rows longer than 16384 vectors are supported with a "
                                            "16-bit output only");

@@ -104,8 +104,9 @@ def candidates(nvec: int, full: bool = True) -> list[str]:
         vpt16 = -(-n16 // 32)
         if vpt16 in warp_vpts:
             out += [f"warp:vec16:vpt{vpt16}:tpr32:cluster1:rpc{r}" for r in (4, 8)]
-    if nvec > 8 * 2048:  # two passes, one CTA or a cluster per row
-        out += [f"twopass:vec32:vpt4:tpr{t}:cluster{cl}:rpc1" for cl in (1, 2, 4, 8) for t in (256, 512)]
+    if nvec > 4096:  # two passes, one CTA or a cluster per row
+        out += [f"twopass:vec32:vpt4:tpr{t}:cluster{cl}:rpc1" for cl in (1, 2, 4, 8)
+                for t in (128, 256, 512)]
     return out
 
 

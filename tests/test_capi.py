@@ -42,7 +42,7 @@ def test_version_and_status_strings():
 @pytest.mark.parametrize("rows,hidden,kind", [
     (4096, 1024, "warp"), (4096, 2048, "cta"), (4096, 4096, "cta"), (4096, 8192, "cta"),
     (4096, 16384, "cta"), (4096, 32768, "cta"), (1, 8192, "cta"), (4, 65536, "cluster"),
-    (4, 1 << 18, "cluster"), (3, 1 << 22, "twopass"),
+    (4, 1 << 18, "twopass"), (4, 40960, "cluster"), (3, 1 << 22, "twopass"),
 ])
 def test_plan_kinds(rows, hidden, kind):
     p = capi.plan(rows, hidden)
@@ -65,9 +65,9 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     # vectors per CTA, else two (the long-row sweep's fit)
     (40960, "cluster:vec32:vpt1:tpr320:cluster8:rpc1"),
     (65536, "cluster:vec32:vpt1:tpr512:cluster8:rpc1"),
-    (98304, "cluster:vec32:vpt2:tpr384:cluster8:rpc1"),
-    (131072, "cluster:vec32:vpt2:tpr512:cluster8:rpc1"),
-    (262144, "cluster:vec32:vpt2:tpr1024:cluster8:rpc1"),
+    (98304, "twopass:vec32:vpt4:tpr512:cluster1:rpc1"),
+    (131072, "twopass:vec32:vpt4:tpr128:cluster8:rpc1"),
+    (262144, "twopass:vec32:vpt4:tpr128:cluster8:rpc1"),
     (262160, "twopass:vec32:vpt4:tpr256:cluster8:rpc1"),
     # short rows: several rows per warp, one vector per lane
     (16, "warp:vec32:vpt1:tpr1:cluster1:rpc256"),
