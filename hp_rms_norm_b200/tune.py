@@ -9,7 +9,11 @@
 
 Times every compiled launch plan that covers each requested shape (through
 ``hprn_set_plan_override``) and prints the fastest, next to the built-in
-heuristic's choice.  Timing: a CUDA graph of back-to-back launches over
+heuristic's choice.  Candidates: warp rows (one warp per row, or several
+short rows per warp), one CTA per row and clusters of 2/4/8 CTAs at 32-byte
+vectors, one CTA per row at 16-byte vectors, two passes (one CTA or a
+cluster per row) past 4096 vectors, and TMA-staged rows (unless
+``--no-tma``).  ``--copy`` also times torch's ``copy_`` of the same bytes.  Timing: a CUDA graph of back-to-back launches over
 rotating buffer sets of at least 600 MB, so every launch reads cold data (or
 one buffer set with ``--warm``), replayed three times after one warm replay;
 with ``--isolated``, the median of single launches each preceded by an L2
