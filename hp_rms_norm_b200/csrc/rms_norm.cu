@@ -112,9 +112,14 @@ int extended_vpt(int nvec, bool residual, int out) {
   switch (out) {
     case kOutSame: return nvec <= 128 ? 0 : (nvec <= 256 ? 1 : 2);
     case kOutFp8Static: return nvec <= 128 ? 0 : (nvec <= 1024 ? 2 : 4);
+    // fp8 with per-row or per-group scales: two vectors per thread up to 512
+    // (the dynamic form then holds its products across the reduction; 4096 x
+    // 6144-8192: 15.6 / 19.1 vs 16.8 / 20.2 us at four), four past it.
     case kOutFp8Dynamic:
-    case kOutFp8Group: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
-    default: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);  // NVFP4 (past 1536: a cluster)
+    case kOutFp8Group: return nvec <= 128 ? 1 : (nvec <= 512 ? 2 : 4);
+    // NVFP4: at 4096 x 32768, one 512-thread CTA at four vectors per thread
+    // takes 62.8 us (83 us for a 4-CTA cluster).
+    default: return nvec <= 128 ? 1 : (nvec <= 256 ? 2 : 4);
   }
 }
 
@@ -158,15 +163,6 @@ Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
     p.vpt = 3;
     p.tpr = 32;
     p.rows_per_cta = 4;
-    return p;
-  }
-  if (!residual && out == kOutNvfp4 && nvec > 1536 && nvec <= 2048) {
-    // Plain NVFP4 rows of 1537..2048 vectors: a 4-CTA cluster at four vectors
-    // per thread beat every one-CTA plan (88 vs 94 us at 4096 x 32768).
-    p.kind = kClusterRows;
-    p.cluster = 4;
-    p.vpt = 4;
-    p.tpr = round_up(((nvec + 3) / 4 + 3) / 4, 32);
     return p;
   }
   if (ext > 0) {

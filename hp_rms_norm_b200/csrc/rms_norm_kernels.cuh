@@ -96,10 +96,12 @@ struct RmsArgs {
 };
 
 // Element pairs go through Blackwell's packed fp32 instructions
-// (__fadd2_rn / __fmul2_rn / __ffma2_rn: add/mul/fma.rn.f32x2).  Each lane
-// rounds exactly as the scalar fp32 instruction does (nearest even, no flush
-// to zero), so the results are those of scalar code, bit for bit, at half the
-// arithmetic instructions.
+// (__fadd2_rn / __fmul2_rn / __ffma2_rn: add/mul/fma.rn.f32x2), and squares
+// and products of two 16-bit operands through its mixed-precision
+// fma.rn.f32.{bf16,f16} (fma_pair / mul_pair), which reads the 16-bit halves
+// directly instead of unpacking them.  Each rounds exactly as the scalar fp32
+// instruction does (nearest even, no flush to zero), so the results are those
+// of scalar code, bit for bit, in fewer instructions.
 
 // Adds residual into input in fp32, keeps the rounded sum in `xv`, and
 // accumulates the squares of the unrounded sums (even elements into a0, odd
@@ -132,10 +134,7 @@ __device__ __forceinline__ void square_sum(const Vec<VEC>& xv, float& a0, float&
   } else {
     float2 acc = make_float2(a0, a1);
 #pragma unroll
-    for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-      const float2 a = unpack2<T>(xv.w[k]);
-      acc = __ffma2_rn(a, a, acc);
-    }
+    for (int k = 0; k < Vec<VEC>::kWords; ++k) acc = fma_pair<T>(xv.w[k], xv.w[k], acc);
     a0 = acc.x;
     a1 = acc.y;
   }
@@ -151,64 +150,65 @@ __device__ __forceinline__ Vec<VEC> normalize(const Vec<VEC>& rv, const Vec<VEC>
     const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
     for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-      const float2 y = __fmul2_rn(__fmul2_rn(unpack2<T>(rv.w[k]), unpack2<T>(wv.w[k])), inv2);
+      const float2 y = __fmul2_rn(mul_pair<T>(rv.w[k], wv.w[k]), inv2);
       o.w[k] = pack2<T>(y.x, y.y);
     }
   }
   return o;
 }
 
-// max_j |f32(r_j) * f32(w_j)| over one vector, folded into m (NaNs are
-// ignored, as by fmaxf).  The row's amax of y_j = (r_j * w_j) * inv is this
-// times inv, rounded once: inv > 0 and round-to-nearest is monotone, so
-// max_j |RN(p_j * inv)| = RN(max_j |p_j| * inv) exactly, with one multiply
-// per row instead of one per element.
+// f32(r_j) * f32(w_j) for the elements of one vector, as pairs: the common
+// factor of every quantised output.  Computed once per element and shared by
+// the amax and the quantiser.
+template <int VEC>
+struct Prod {
+  float2 p[Vec<VEC>::kWords];
+};
+
 template <typename T, int VEC>
-__device__ __forceinline__ float vec_amax_rw(const Vec<VEC>& rv, const Vec<VEC>& wv, float m) {
+__device__ __forceinline__ Prod<VEC> product(const Vec<VEC>& rv, const Vec<VEC>& wv) {
+  Prod<VEC> o;
 #pragma unroll
-  for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-    const float2 p = __fmul2_rn(unpack2<T>(rv.w[k]), unpack2<T>(wv.w[k]));
-    m = fmaxf(m, fmaxf(fabsf(p.x), fabsf(p.y)));
-  }
+  for (int k = 0; k < Vec<VEC>::kWords; ++k) o.p[k] = mul_pair<T>(rv.w[k], wv.w[k]);
+  return o;
+}
+
+// max(m, |a|, |b|) in one sm_100 three-input max.f32.  NaN operands are
+// ignored, as by fmaxf; no flush to zero.
+__device__ __forceinline__ float max_abs2(float m, float a, float b) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(m), "f"(fabsf(a)), "f"(fabsf(b)));
+  return d;
+}
+
+// max_j |p_j| over one vector of products, folded into m.  The amax of
+// y_j = p_j * inv is this times inv, rounded once: inv > 0 and
+// round-to-nearest is monotone, so max_j |RN(p_j * inv)| = RN(max_j |p_j| * inv)
+// exactly, with one multiply per row (or group) instead of one per element.
+template <int VEC>
+__device__ __forceinline__ float prod_amax(const Prod<VEC>& p, float m) {
+#pragma unroll
+  for (int k = 0; k < Vec<VEC>::kWords; ++k) m = max_abs2(m, p.p[k].x, p.p[k].y);
   return m;
 }
 
-// square_sum and vec_amax_rw over one input vector in one pass (plain rows
-// with a dynamic fp8 scale), unpacking each pair once for both.
-template <typename T, int VEC>
-__device__ __forceinline__ float square_sum_amax(const Vec<VEC>& xv, const Vec<VEC>& wv, float& a0,
-                                                 float& a1, float m) {
-  float2 acc = make_float2(a0, a1);
-#pragma unroll
-  for (int k = 0; k < Vec<VEC>::kWords; ++k) {
-    const float2 x = unpack2<T>(xv.w[k]);
-    acc = __ffma2_rn(x, x, acc);
-    const float2 p = __fmul2_rn(x, unpack2<T>(wv.w[k]));
-    m = fmaxf(m, fmaxf(fabsf(p.x), fabsf(p.y)));
-  }
-  a0 = acc.x;
-  a1 = acc.y;
-  return m;
-}
-
-// e4m3_satfinite((f32(r) * f32(w) * inv) * inv_scale) for one vector: VEC/2
+// e4m3_satfinite((p * inv) * inv_scale) for one vector of products: VEC/2
 // output bytes, element order preserved.
-template <typename T, int VEC>
-__device__ __forceinline__ Vec<VEC / 2> quantize_e4m3(const Vec<VEC>& rv, const Vec<VEC>& wv,
-                                                      float inv, float inv_scale) {
+template <int VEC>
+__device__ __forceinline__ Vec<VEC / 2> quantize_e4m3(const Prod<VEC>& p, float inv,
+                                                      float inv_scale) {
   static_assert(VEC >= 8, "fp8 output needs at least 4 elements per vector");
   Vec<VEC / 2> o;
-#pragma unroll
   const float2 inv2 = make_float2(inv, inv);
   const float2 is2 = make_float2(inv_scale, inv_scale);
+#pragma unroll
   for (int k = 0; k < Vec<VEC>::kWords; k += 2) {
     uint32_t word = 0;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float2 y = __fmul2_rn(__fmul2_rn(unpack2<T>(rv.w[k + h]), unpack2<T>(wv.w[k + h])), inv2);
-      const float2 q = __fmul2_rn(y, is2);
-      const __nv_fp8x2_storage_t p = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
-      word |= static_cast<uint32_t>(p) << (16 * h);
+      const float2 q = __fmul2_rn(__fmul2_rn(p.p[k + h], inv2), is2);
+      const __nv_fp8x2_storage_t b = __nv_cvt_float2_to_fp8x2(q, __NV_SATFINITE, __NV_E4M3);
+      word |= static_cast<uint32_t>(b) << (16 * h);
     }
     o.w[k / 2] = word;
   }
@@ -227,8 +227,8 @@ __device__ __forceinline__ Vec<8> quantize_nvfp4(const Vec<32>& rv, const Vec<32
   float amax = 0.f;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    y[k] = __fmul2_rn(__fmul2_rn(unpack2<T>(rv.w[k]), unpack2<T>(wv.w[k])), inv2);
-    amax = fmaxf(amax, fmaxf(fabsf(y[k].x), fabsf(y[k].y)));
+    y[k] = __fmul2_rn(mul_pair<T>(rv.w[k], wv.w[k]), inv2);
+    amax = max_abs2(amax, y[k].x, y[k].y);
   }
   const __nv_fp8_storage_t sf = __nv_cvt_float_to_fp8(gs * (amax / 6.0f), __NV_SATFINITE, __NV_E4M3);
   const float sfv = __half2float(__half(__nv_cvt_fp8_to_halfraw(sf, __NV_E4M3)));
@@ -322,6 +322,14 @@ __device__ __forceinline__ float static_inv_scale(const RmsArgs& a) {
   return 1.0f;
 }
 
+// Writes the e4m3 codes of one output vector from its products.
+template <int VEC>
+__device__ __forceinline__ void store_e4m3(const RmsArgs& a, int64_t row, int64_t v,
+                                           const Prod<VEC>& p, float inv, float inv_scale) {
+  uint8_t* o = static_cast<uint8_t*>(a.out) + row * a.out_stride + v * Vec<VEC>::kElems;
+  st_global<VEC / 2>(o, quantize_e4m3<VEC>(p, inv, inv_scale));
+}
+
 // Writes one output vector of row `row` at vector index v.
 template <typename T, int VEC, int OUT>
 __device__ __forceinline__ void store_out(const RmsArgs& a, int64_t row, int64_t v,
@@ -339,8 +347,7 @@ __device__ __forceinline__ void store_out(const RmsArgs& a, int64_t row, int64_t
     st_global<8>(o, quantize_nvfp4<T>(rv, wv, inv, inv_scale, &sf));
     a.block_scales[row * a.nvec + v] = sf;
   } else {
-    uint8_t* o = static_cast<uint8_t*>(a.out) + row * a.out_stride + v * EPV;
-    st_global<VEC / 2>(o, quantize_e4m3<T, VEC>(rv, wv, inv, inv_scale));
+    store_e4m3<VEC>(a, row, v, product<T, VEC>(rv, wv), inv, inv_scale);
   }
 }
 
@@ -371,25 +378,40 @@ __device__ __forceinline__ float pow2_ceil(float s) {
 // (vector index = a group-aligned base + lane), so the group amax is a
 // butterfly over log2(group_vecs) lanes: every lane of the warp must call
 // this, lanes outside the slice with in = false.  max |y| over a vector is
-// max |r * w| times inv, rounded once (exact, see vec_amax_rw).
+// max |r * w| times inv, rounded once (exact, see prod_amax); the products
+// are formed once for the amax and the quantiser.
 template <typename T, int VEC, bool RES>
 __device__ __forceinline__ void store_group_fp8(const RmsArgs& a, int64_t row, int v, bool in,
                                                 const Vec<VEC>& rv, const Vec<VEC>& held,
                                                 float inv, uint64_t pol_keep) {
-  constexpr int EPV = Vec<VEC>::kElems;
   Vec<VEC> wv = held;
   if (!RES && in) wv = weight_vec<VEC, RES>(a, v, held, pol_keep);
-  float m = in ? vec_amax_rw<T, VEC>(rv, wv, 0.f) * inv : 0.f;
-  for (int o = 1; o < a.group_vecs; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const Prod<VEC> p = product<T, VEC>(rv, wv);
+  float m = in ? prod_amax<VEC>(p, 0.f) * inv : 0.f;
+  // group_vecs is 2, 4 or 8 (groups of 32/64/128 elements, 16 per vector).
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1)
+    if (o < a.group_vecs) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float scale = fmaxf(m, kMinAmax) / kE4m3Max;
   if (a.scale_pow2) scale = pow2_ceil(scale);
   if (in) {
-    uint8_t* o = static_cast<uint8_t*>(a.out) + row * a.out_stride + static_cast<int64_t>(v) * EPV;
-    st_global<VEC / 2>(o, quantize_e4m3<T, VEC>(rv, wv, inv, 1.0f / scale));
-    if (v % a.group_vecs == 0)
-      a.row_scales[row * a.gs_row + static_cast<int64_t>(v / a.group_vecs) * a.gs_group] = scale;
+    store_e4m3<VEC>(a, row, v, p, inv, 1.0f / scale);
+    if ((v & (a.group_vecs - 1)) == 0) {  // the group's first vector; v >= 0
+      const int g = v >> (__ffs(a.group_vecs) - 1);
+      a.row_scales[row * a.gs_row + static_cast<int64_t>(g) * a.gs_group] = scale;
+    }
   }
 }
+
+// Whether a dynamic-fp8 kernel keeps the fp32 products r * w (16 registers
+// per 32-byte vector) live across the row reduction, so that the output pass
+// only scales, converts and stores, instead of keeping the 16-bit row (8
+// registers) and forming the products a second time.  A fused row holds r
+// and w across the reduction anyway, so its products cost no extra
+// registers.  A plain row holds only x: at up to two vectors per thread the
+// products fit beside it (4096 x 8192: 19.0 vs 20.9 us), at four they cost
+// half the resident CTAs (4096 x 32768: 89 vs 72 us).
+__host__ __device__ constexpr bool hold_products(bool res, int vpt) { return res || vpt <= 2; }
 
 // ---------------------------------------------------------------------------
 // Kernel 1: rows of at most 4 * 32 vectors, each held by `lanes_per_row`
@@ -422,8 +444,12 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   }
   float a0 = 0.f, a1 = 0.f;
   // Dynamic fp8: max |r * w| does not depend on inv, so it is reduced next to
-  // the sum of squares and scaled by inv once (see vec_amax_rw); plain rows
-  // take it in the same pass as the sum of squares.
+  // the sum of squares and scaled by inv once (see prod_amax).  The products
+  // r * w are held across the reduction for the output pass (kHold, see
+  // hold_products).
+  constexpr bool kAmax = OUT == kOutFp8Dynamic;
+  constexpr bool kHold = kAmax && hold_products(RES, VPT);
+  Prod<kHold ? VEC : 8> pv[VPT];
   float m = 0.f;
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
@@ -432,20 +458,25 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
       if constexpr (RES) {
         add_round<T, VEC>(xv[j], rv[j], a0, a1);
         st_global<VEC>(rr + v * EPV, xv[j]);
-      } else if constexpr (OUT == kOutFp8Dynamic) {
-        m = square_sum_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), a0, a1, m);
+        wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
       } else {
         square_sum<T, VEC>(xv[j], a0, a1);
+        if constexpr (kAmax) {
+          const Prod<VEC> p = product<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep));
+          m = prod_amax<VEC>(p, m);
+          if constexpr (kHold) pv[j] = p;
+        }
       }
-      if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + v * EPV, pol_keep);
     }
   }
-  if constexpr (RES && OUT == kOutFp8Dynamic) {
+  if constexpr (RES && kAmax) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = sub + lpr * j;
-      if (active && v < a.nvec)
-        m = vec_amax_rw<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), m);
+      if (active && v < a.nvec) {
+        pv[j] = product<T, VEC>(xv[j], wv[j]);
+        m = prod_amax<VEC>(pv[j], m);
+      }
     }
   }
   const float inv = rsqrtf(fmaf(lane_group_sum(a0 + a1, lpr), a.inv_hidden, a.eps));
@@ -460,6 +491,8 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
     const int v = sub + lpr * j;
     if constexpr (OUT == kOutFp8Group) {
       store_group_fp8<T, VEC, RES>(a, row, v, active && v < a.nvec, xv[j], wv[j], inv, pol_keep);
+    } else if constexpr (kHold) {
+      if (active && v < a.nvec) store_e4m3<VEC>(a, row, v, pv[j], inv, inv_scale);
     } else if (active && v < a.nvec) {
       store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
                              inv_scale);
@@ -475,6 +508,15 @@ __host__ __device__ constexpr int cta_max_threads(int vpt) {
   return vpt <= 2 ? 1024 : (vpt <= 4 ? 512 : 256);
 }
 
+// CTAs of cta_max_threads(VPT) threads each SM must hold at once (0: no
+// minimum, the compiler's own register choice).  A plain
+// 16-bit row at two vectors per thread (one CTA per row) runs in 1024-thread
+// CTAs at hidden 32768 and needs two of them per SM, i.e. at most 32
+// registers per thread (with 33 it ran at 0.83 of the copy peak, not 1.01).
+__host__ __device__ constexpr int cta_min_blocks(int vpt, bool cluster, bool res, int out) {
+  return (vpt == 2 && !cluster && !res && out == kOutSame) ? 2 : 0;
+}
+
 // ---------------------------------------------------------------------------
 // Kernel 2: one CTA per row slice; with CLUSTER, the row is split over the
 // CTAs of a thread-block cluster (launched with cluster dims (n, 1, 1)) and
@@ -483,7 +525,8 @@ __host__ __device__ constexpr int cta_max_threads(int vpt) {
 // locally after one cluster barrier and no CTA touches a peer's memory
 // afterwards.
 template <typename T, int VEC, int VPT, bool CLUSTER, bool RES, int OUT>
-__global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArgs a) {
+__global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUSTER, RES, OUT))
+    rms_norm_cta_rows(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
   __shared__ float warp_part[32];
   __shared__ float warp_amax[32];
@@ -527,9 +570,11 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
   }
   // Dynamic fp8: max |r * w| does not depend on inv, so it travels with the
   // sum of squares through the same barrier (and cluster phase) and is scaled
-  // by inv once at the end (see vec_amax_rw); plain rows take it in the same
-  // pass as the sum of squares.
+  // by inv once at the end (see prod_amax).  The products r * w are held
+  // across the reduction for the output pass (kHold, see hold_products).
   constexpr bool kAmax = OUT == kOutFp8Dynamic;
+  constexpr bool kHold = kAmax && hold_products(RES, VPT);
+  Prod<kHold ? VEC : 8> pv[VPT];
   float a0 = 0.f, a1 = 0.f;
   float m = 0.f;
 #pragma unroll
@@ -539,19 +584,25 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
       if constexpr (RES) {
         add_round<T, VEC>(xv[j], rv[j], a0, a1);
         st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
-      } else if constexpr (kAmax) {
-        m = square_sum_amax<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), a0, a1, m);
+        wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
       } else {
         square_sum<T, VEC>(xv[j], a0, a1);
+        if constexpr (kAmax) {
+          const Prod<VEC> p = product<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep));
+          m = prod_amax<VEC>(p, m);
+          if constexpr (kHold) pv[j] = p;
+        }
       }
-      if constexpr (RES) wv[j] = ld_weight<VEC>(a.w + static_cast<int64_t>(v) * EPV, pol_keep);
     }
   }
   if constexpr (RES && kAmax) {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = v_begin + tid + j * nthreads;
-      if (v < v_end) m = vec_amax_rw<T, VEC>(xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), m);
+      if (v < v_end) {
+        pv[j] = product<T, VEC>(xv[j], wv[j]);
+        m = prod_amax<VEC>(pv[j], m);
+      }
     }
   }
   const float wsum = warp_sum(a0 + a1);
@@ -587,6 +638,8 @@ __global__ void __launch_bounds__(cta_max_threads(VPT)) rms_norm_cta_rows(RmsArg
     const int v = v_begin + tid + j * nthreads;
     if constexpr (OUT == kOutFp8Group) {
       store_group_fp8<T, VEC, RES>(a, row, v, v < v_end, xv[j], wv[j], inv, pol_keep);
+    } else if constexpr (kHold) {
+      if (v < v_end) store_e4m3<VEC>(a, row, v, pv[j], inv, inv_scale);
     } else if (v < v_end) {
       store_out<T, VEC, OUT>(a, row, v, xv[j], weight_vec<VEC, RES>(a, v, wv[j], pol_keep), inv,
                              inv_scale);

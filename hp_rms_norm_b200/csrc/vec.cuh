@@ -246,6 +246,44 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
   return __half22float2(h);
 }
 
+// {lo(a) * lo(b) + c.x, hi(a) * hi(b) + c.y} for 16-bit pairs a and b (bf16
+// or fp16) with fp32 addends and results: sm_100's mixed-precision
+// fma.rn.f32.{bf16,f16}.  The 16-bit operands widen to fp32 exactly and each
+// element is rounded once, so the results are those of fmaf on the unpacked
+// values, bit for bit, without the unpacking.
+template <typename T>
+__device__ __forceinline__ float2 fma_pair(uint32_t a, uint32_t b, float2 c);
+
+template <>
+__device__ __forceinline__ float2 fma_pair<__nv_bfloat16>(uint32_t a, uint32_t b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\tmov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %4;\n\tfma.rn.f32.bf16 %1, ah, bh, %5;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+template <>
+__device__ __forceinline__ float2 fma_pair<__half>(uint32_t a, uint32_t b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %2;\n\tmov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, al, bl, %4;\n\tfma.rn.f32.f16 %1, ah, bh, %5;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "r"(a), "r"(b), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// {lo(a) * lo(b), hi(a) * hi(b)} in fp32: exact, since a product of two
+// 16-bit floats has at most 22 significant bits.  Adding -0 leaves every
+// product, a zero's sign included, as fmul rounds it.
+template <typename T>
+__device__ __forceinline__ float2 mul_pair(uint32_t a, uint32_t b) {
+  return fma_pair<T>(a, b, make_float2(-0.0f, -0.0f));
+}
+
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi);
 
