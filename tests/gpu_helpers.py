@@ -71,3 +71,32 @@ def ulp_distance(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
         return torch.where(i < 0, -mag, mag)
 
     return (ordered(a) - ordered(b)).abs()
+
+
+def edge_operands(code: int, hidden: int, seed: int):
+    """16-bit bit patterns for the products r * w: rows of subnormal inputs
+    (both signs), signed zeros, large values, and ordinary values; and a
+    weight with subnormal and signed-zero entries.  The large values (2^14
+    in fp16, 2^57 in bf16) keep the fused row's sums and the fp32 sum of
+    squares finite, which the oracle's double-precision sum would not
+    mirror."""
+    g = np.random.default_rng(seed)
+    sub_max = 0x03FF if code == O.FP16 else 0x007F   # largest subnormal magnitude
+    big = 0x7400 if code == O.FP16 else 0x5C00
+    sign = lambda n: (g.integers(0, 2, n) << 15).astype(np.uint16)
+    x = np.empty((5, hidden), dtype=np.uint16)
+    x[0] = g.integers(1, sub_max + 1, hidden).astype(np.uint16) | sign(hidden)
+    x[1] = sign(hidden)                                               # +0 / -0
+    x[2] = np.where(g.random(hidden) < 0.5, 0x3C00 if code == O.FP16 else 0x3F80, big)
+    x[2] |= sign(hidden)
+    x[3] = (g.integers(0x2000, 0x4400, hidden) if code == O.FP16
+            else g.integers(0x3800, 0x4080, hidden)).astype(np.uint16) | sign(hidden)
+    x[4] = np.where(g.random(hidden) < 0.5, x[0], x[3])
+    w_plain = (g.integers(0x3A00, 0x3E00, hidden) if code == O.FP16
+               else g.integers(0x3F40, 0x3FC0, hidden)).astype(np.uint16)
+    w_edge = w_plain.copy()
+    k = g.permutation(hidden)
+    w_edge[k[: hidden // 4]] = g.integers(1, sub_max + 1, hidden // 4).astype(np.uint16)
+    w_edge[k[hidden // 4: hidden // 2]] = sign(hidden // 4)           # +0 / -0 weights
+    w_edge[k[hidden // 2:]] |= sign(hidden - hidden // 2)
+    return x, w_plain, w_edge

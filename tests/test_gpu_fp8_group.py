@@ -12,7 +12,7 @@ import torch
 import hp_rms_norm_b200 as H
 from hp_rms_norm_b200 import capi
 from oracle import oracle as O
-from tests.gpu_helpers import DTYPES, bits
+from tests.gpu_helpers import DTYPES, bits, edge_operands, from_bits
 from tests.numerics import assert_bits_equal
 
 pytestmark = pytest.mark.gpu
@@ -107,6 +107,21 @@ def test_forced_plans_vs_oracle(cuda, residual, rows, hidden, plan):
         check(x, w, rr, 1e-6, O.BF16, 128, False, plan, run_capi(x, w, rr, 1e-6, 128, False))
     finally:
         capi.set_plan_override(None)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("residual", [True, False])
+@pytest.mark.parametrize("group", [32, 128])
+def test_edge_operands_vs_oracle(cuda, dtype, residual, group):
+    """Subnormal inputs and weights, signed zeros and large values (the
+    products r * w are formed without unpacking the 16-bit operands)."""
+    tdtype, code = DTYPES[dtype]
+    x, w_plain, w_edge = edge_operands(code, 4096, 13 + code)
+    for wname, wb in (("weight", w_plain), ("edge weight", w_edge)):
+        xt, wt = from_bits(x, tdtype, cuda), from_bits(wb, tdtype, cuda)
+        rt = from_bits(x[::-1].copy(), tdtype, cuda) if residual else None
+        check(xt, wt, rt, 1e-30, code, group, False, f"{dtype} {wname} g{group} res={residual}",
+              run_capi(xt, wt, rt, 1e-30, group, False))
 
 
 def test_torch_op_column_major_scales_and_3d(cuda):

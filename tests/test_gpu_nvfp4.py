@@ -11,7 +11,7 @@ import torch
 import hp_rms_norm_b200
 from hp_rms_norm_b200 import capi
 from oracle import oracle as O
-from tests.gpu_helpers import DTYPES, bits, make_inputs
+from tests.gpu_helpers import DTYPES, bits, edge_operands, from_bits, make_inputs
 from tests.numerics import assert_bits_equal
 
 pytestmark = pytest.mark.gpu
@@ -56,6 +56,29 @@ def test_nvfp4_vs_oracle(cuda, rows, hidden, residual, dtype):
     if residual:
         assert_bits_equal(bits(r), want_res, code, label=label + " residual")
     check_nvfp4(q.cpu().numpy(), sf.cpu().numpy(), want_q, want_sf, label)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("residual", [False, True])
+def test_nvfp4_edge_operands_vs_oracle(cuda, residual, dtype):
+    """Subnormal inputs and weights, signed zeros and large values (the
+    products r * w are formed without unpacking the 16-bit operands)."""
+    tdtype, code = DTYPES[dtype]
+    x, w_plain, w_edge = edge_operands(code, 4096, 11 + code)
+    for wname, wb in (("weight", w_plain), ("edge weight", w_edge)):
+        rb = x[::-1].copy()
+        xt, wt, rt = (from_bits(a, tdtype, cuda) for a in (x, wb, rb))
+        want_q, want_sf, want_res = O.rms_norm_nvfp4(code, x, wb, 1e-30, GS,
+                                                     r=rb if residual else None)
+        q = torch.empty(5, 2048, dtype=torch.uint8, device=cuda)
+        sf = torch.empty(5, 256, dtype=torch.uint8, device=cuda)
+        capi.rms_norm_nvfp4_tensors(q, sf, xt, wt, rt if residual else None, 1e-30,
+                                    torch.tensor([GS], device=cuda))
+        torch.cuda.synchronize()
+        label = f"{dtype} {wname} residual={residual}"
+        if residual:
+            assert_bits_equal(bits(rt), want_res, code, label=label + " residual")
+        check_nvfp4(q.cpu().numpy(), sf.cpu().numpy(), want_q, want_sf, label)
 
 
 def test_nvfp4_torch_op_matches_capi(cuda):

@@ -14,7 +14,7 @@ import torch
 import hp_rms_norm_b200
 from hp_rms_norm_b200 import capi
 from oracle import oracle as O
-from tests.gpu_helpers import DTYPES, bits, make_inputs
+from tests.gpu_helpers import DTYPES, bits, edge_operands, from_bits, make_inputs
 from tests.numerics import assert_bits_equal, assert_output_close
 
 pytestmark = pytest.mark.gpu
@@ -110,6 +110,30 @@ def test_variant_every_plan_kind(cuda, variant, rows, hidden, plan):
         check_variant(variant, x, w, r, eps, O.BF16, cuda, f"{variant} {plan}")
     finally:
         capi.set_plan_override(None)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_edge_operands_vs_oracle(cuda, variant, dtype):
+    """Products and squares of 16-bit operands are exact in fp32 and must not
+    flush subnormal operands or lose a zero's sign: subnormal inputs and
+    weights, signed zeros and the largest finite values against the oracle.
+    eps is tiny so that the subnormal rows' own sums of squares set their
+    scale."""
+    tdtype, code = DTYPES[dtype]
+    hidden = 4096
+    x, w_plain, w_edge = edge_operands(code, hidden, 7 + code)
+    for wname, wb in (("weight", w_plain), ("edge weight", w_edge)):
+        xt = from_bits(x, tdtype, cuda)
+        wt = from_bits(wb, tdtype, cuda)
+        rt = from_bits(x[::-1].copy(), tdtype, cuda)
+        check_variant(variant, xt, wt, rt, 1e-30, code, cuda, f"{variant} {dtype} {wname}")
+        if variant == "plain16":
+            # The signed-zero row: y = (x * w) * inv is a zero whose sign is
+            # sign(x) xor sign(w), bit for bit.
+            want_out, _, _ = O.rms_norm_out(code, x, wb, 1e-30)
+            out, _, _ = run_variant(variant, xt, wt, rt, 1e-30, cuda)
+            assert np.array_equal(bits(out)[1], want_out[1]), f"{dtype} {wname}: signed zeros"
 
 
 @pytest.mark.parametrize("hidden", [3, 7, 129, 4097])
