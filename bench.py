@@ -559,9 +559,58 @@ def run_e2e(args, shapes, bufs, stream, dev, dist, eps):
     torch.cuda.synchronize()
     ms = dist.max(t0.elapsed_time(t1), dev) / K
     total = sum(alg_bytes(rows, h) for rows, h in shapes) * dist.world
-    return {"value": round(total / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+    value = total / (ms / 1e3) / 1e9
+    link = pcie_ceiling(dev)
+    return {"value": round(value, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
-            "steps": K, "api": "hprn_rms_norm (C ABI) on pinned-host-staged buffers, 3 streams"}
+            "steps": K, "api": "hprn_rms_norm (C ABI) on pinned-host-staged buffers, 3 streams",
+            "roofline": {"bound": "pcie", "achieved": round(value / dist.world, 2),
+                         "peak": link["bidirectional_gbs"], "unit": "GB/s",
+                         "frac": round(value / dist.world / link["bidirectional_gbs"], 3),
+                         "peak_source": "measured here: " + link["how"], **link}}
+
+
+def pcie_ceiling(dev, nbytes=1 << 30, reps=3):
+    """Host<->device copy bandwidth of this GPU's link, measured live: pinned
+    buffers of `nbytes`, H2D alone, D2H alone, and both at once on two streams
+    (the bound of the end-to-end number, whose steps move as many bytes each
+    way)."""
+    import torch
+
+    n = nbytes // 2
+    h_in = torch.empty(n, dtype=torch.bfloat16).pin_memory()
+    h_out = torch.empty(n, dtype=torch.bfloat16).pin_memory()
+    d_a = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    d_b = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    s1, s2 = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps / 1e3
+
+    def both():
+        main = torch.cuda.current_stream()
+        s1.wait_stream(main)
+        s2.wait_stream(main)
+        with torch.cuda.stream(s1):
+            d_a.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(s2):
+            h_out.copy_(d_b, non_blocking=True)
+        main.wait_stream(s1)
+        main.wait_stream(s2)
+
+    h2d = nbytes / timed(lambda: d_a.copy_(h_in, non_blocking=True)) / 1e9
+    d2h = nbytes / timed(lambda: h_out.copy_(d_b, non_blocking=True)) / 1e9
+    bi = 2 * nbytes / timed(both) / 1e9
+    return {"h2d_gbs": round(h2d, 1), "d2h_gbs": round(d2h, 1), "bidirectional_gbs": round(bi, 1),
+            "how": f"pinned {nbytes >> 20} MiB copies, both directions at once on two streams"}
 
 
 VARIANT_HIDDEN = [2048, 4096, 8192, 16384, 32768]
