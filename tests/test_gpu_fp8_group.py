@@ -124,6 +124,22 @@ def test_edge_operands_vs_oracle(cuda, dtype, residual, group):
               run_capi(xt, wt, rt, 1e-30, group, False))
 
 
+@pytest.mark.parametrize("weight_special", [None, "nan", "inf"])
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("residual", [True, False])
+def test_nonfinite_vs_oracle(cuda, dtype, residual, weight_special):
+    """NaN and infinities inside groups and in the weight (group amaxes
+    ignore NaN as fmaxf does)."""
+    from tests.test_gpu_rms_norm_variants import nonfinite_rows
+
+    tdtype, code = DTYPES[dtype]
+    x, r, w = nonfinite_rows(code, 4096, 5 + code, weight_special)
+    xt, rt, wt = (from_bits(a, tdtype, cuda) for a in (x, r, w))
+    rr = rt if residual else None
+    check(xt, wt, rr, 1e-6, code, 128, False, f"{dtype} non-finite res={residual}",
+          run_capi(xt, wt, rr, 1e-6, 128, False))
+
+
 def test_torch_op_column_major_scales_and_3d(cuda):
     x, w, r = _inputs(6 * 7, 2048, torch.bfloat16, 5, cuda)
     x3, r3 = x.view(6, 7, 2048), r.clone().view(6, 7, 2048)

@@ -136,6 +136,41 @@ def test_edge_operands_vs_oracle(cuda, variant, dtype):
             assert np.array_equal(bits(out)[1], want_out[1]), f"{dtype} {wname}: signed zeros"
 
 
+def nonfinite_rows(code, hidden, seed, weight_special=None):
+    """Rows of ordinary values with NaN, +inf and -inf planted, and a clean
+    row; with weight_special "nan" or "inf", two weight entries are that
+    value, so the clean row's products hold it while its sum of squares stays
+    finite (the amaxes must ignore NaN as fmaxf does)."""
+    g = np.random.default_rng(seed)
+    one, inf, nan = (0x3C00, 0x7C00, 0x7E00) if code == O.FP16 else (0x3F80, 0x7F80, 0x7FC0)
+    x = (g.integers(one - 0x400 if code == O.FP16 else one - 0x80, one + 0x200, (4, hidden))
+         .astype(np.uint16) | (g.integers(0, 2, (4, hidden)) << 15).astype(np.uint16))
+    x[0, 17] = nan
+    x[1, 100] = inf
+    x[2, 5] = inf | 0x8000
+    x[2, 3000] = nan
+    r = (g.integers(one - 0x400 if code == O.FP16 else one - 0x80, one, (4, hidden))
+         .astype(np.uint16))
+    w = g.integers(one - 0x100 if code == O.FP16 else one - 0x20, one + 0x100 if code == O.FP16
+                   else one + 0x20, hidden).astype(np.uint16)
+    if weight_special:
+        w[[7, 2000]] = nan if weight_special == "nan" else inf
+    return x, r, w
+
+
+@pytest.mark.parametrize("weight_special", [None, "nan", "inf"])
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_nonfinite_vs_oracle(cuda, variant, dtype, weight_special):
+    """NaN and infinities inside rows and in the weight: NaN positions,
+    infinities and every finite result as the oracle has them (per-row fp8
+    scales included)."""
+    tdtype, code = DTYPES[dtype]
+    x, r, w = nonfinite_rows(code, 4096, 3 + code, weight_special)
+    xt, rt, wt = (from_bits(a, tdtype, cuda) for a in (x, r, w))
+    check_variant(variant, xt, wt, rt, 1e-6, code, cuda, f"{variant} {dtype} non-finite")
+
+
 @pytest.mark.parametrize("hidden", [3, 7, 129, 4097])
 def test_plain_odd_hidden(cuda, hidden):
     x, w, r, eps = make_inputs(6, hidden, torch.float16, "c0", seed=hidden, device=cuda)
