@@ -65,7 +65,7 @@ bool vpt_supported(Kind k, int vec, int vpt, const Variant& v) {
     switch (k) {
       case kWarpRows: return vpt == 1 || vpt == 2 || vpt == 4;
       case kCtaRows: return vpt == 1 || vpt == 2 || vpt == 4;
-      case kClusterRows: return vpt == 2 || vpt == 4;
+      case kClusterRows: return vpt == 1 || vpt == 2 || vpt == 4;
       default: return v.out == kOutSame;
     }
   }
@@ -107,7 +107,14 @@ int slice_vecs_of(int nvec, int cluster, int out) {
 // vectors per thread in smaller CTAs as rows grow.  Vectors per thread for a
 // one-CTA row of nvec vectors, or 0 for the warp-per-row kernel:
 int extended_vpt(int nvec, bool residual, int out) {
-  if (residual) return out == kOutNvfp4 ? (nvec <= 768 ? 1 : 2) : -1;  // -1: the fused rule
+  // Fused NVFP4: one vector per thread up to 768 vectors, then two, but four
+  // at 1025-1280 vectors: there two vectors per thread need 544-640 threads
+  // at 60 registers (one CTA per SM) and four need at most 320 at 94 (two
+  // per SM); 4096 x 17408 / 20480: 72.8 / 85.0 vs 86.8 / 94.0 us.  Past 1280
+  // both fit one CTA per SM and two vectors win (101.8 vs 107.4 us at
+  // 22528).  -1: the fused 16-bit rule.
+  if (residual)
+    return out == kOutNvfp4 ? (nvec <= 768 ? 1 : (nvec > 1024 && nvec <= 1280 ? 4 : 2)) : -1;
   if (nvec <= 64) return 0;
   switch (out) {
     case kOutSame: return nvec <= 128 ? 0 : (nvec <= 256 ? 1 : 2);
@@ -382,9 +389,7 @@ KernelFn pick_cta(int vpt) {
     if (vpt == 8) return rms_norm_cta_rows<T, VEC, 8, CL, RES, OUT>;
   }
   switch (vpt) {
-    case 1:
-      if constexpr (!CL || (RES && OUT == kOutSame)) return rms_norm_cta_rows<T, VEC, 1, CL, RES, OUT>;
-      return nullptr;
+    case 1: return rms_norm_cta_rows<T, VEC, 1, CL, RES, OUT>;
     case 2: return rms_norm_cta_rows<T, VEC, 2, CL, RES, OUT>;
     case 4: return rms_norm_cta_rows<T, VEC, 4, CL, RES, OUT>;
   }

@@ -88,8 +88,6 @@ def candidates(nvec: int, full: bool = True) -> list[str]:
                 out += [f"warp:vec32:vpt{vpt}:tpr{lanes}:cluster1:rpc{t // lanes}" for t in (128, 256)]
     for cl in (1, 2, 4, 8):
         for vpt in cta_vpts:
-            if cl > 1 and not full and vpt == 1:
-                continue
             max_threads = 1024 if vpt <= 2 else (512 if vpt <= 4 else 256)
             sl = -(-nvec // cl)
             tpr = -(-(-(-sl // vpt)) // 32) * 32

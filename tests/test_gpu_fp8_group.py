@@ -89,6 +89,8 @@ FORCED = [
     (9, 4096, "cta:vec32:vpt1:tpr256:cluster1:rpc1"),
     (9, 4096, "cta:vec32:vpt2:tpr128:cluster1:rpc1"),
     (9, 4096, "cta:vec32:vpt4:tpr64:cluster1:rpc1"),
+    (5, 16384, "cluster:vec32:vpt1:tpr512:cluster2:rpc1"),
+    (5, 24576, "cluster:vec32:vpt1:tpr768:cluster2:rpc1"),
     (5, 4096, "cluster:vec32:vpt2:tpr32:cluster8:rpc1"),
     (5, 4096, "cluster:vec32:vpt4:tpr32:cluster4:rpc1"),
     (5, 1152, "cluster:vec32:vpt2:tpr32:cluster8:rpc1"),

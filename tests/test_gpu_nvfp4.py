@@ -81,6 +81,33 @@ def test_nvfp4_edge_operands_vs_oracle(cuda, residual, dtype):
         check_nvfp4(q.cpu().numpy(), sf.cpu().numpy(), want_q, want_sf, label)
 
 
+@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("rows,hidden,plan", [
+    (9, 4096, "cta:vec32:vpt2:tpr128:cluster1:rpc1"),
+    (9, 8192, "cta:vec32:vpt4:tpr128:cluster1:rpc1"),
+    (5, 24576, "cluster:vec32:vpt1:tpr768:cluster2:rpc1"),
+    (5, 32768, "cluster:vec32:vpt4:tpr128:cluster4:rpc1"),
+    (33, 1024, "warp:vec32:vpt2:tpr32:cluster1:rpc4"),
+])
+def test_nvfp4_forced_plans_vs_oracle(cuda, rows, hidden, plan, residual):
+    """Kernel kinds and vectors-per-thread the heuristic may not pick."""
+    x, w, r, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=hidden + rows, device=cuda)
+    xb, wb, rb = bits(x), bits(w), bits(r)
+    want_q, want_sf, want_res = O.rms_norm_nvfp4(O.BF16, xb, wb, eps, GS, r=rb if residual else None)
+    q = torch.empty(rows, hidden // 2, dtype=torch.uint8, device=cuda)
+    sf = torch.empty(rows, hidden // 16, dtype=torch.uint8, device=cuda)
+    capi.set_plan_override(plan)
+    try:
+        capi.rms_norm_nvfp4_tensors(q, sf, x, w, r if residual else None, eps,
+                                    torch.tensor([GS], device=cuda))
+        torch.cuda.synchronize()
+    finally:
+        capi.set_plan_override(None)
+    if residual:
+        assert_bits_equal(bits(r), want_res, O.BF16, label=plan + " residual")
+    check_nvfp4(q.cpu().numpy(), sf.cpu().numpy(), want_q, want_sf, plan)
+
+
 def test_nvfp4_torch_op_matches_capi(cuda):
     x, w, r, eps = make_inputs(96, 8192, torch.bfloat16, "c2", seed=4, device=cuda)
     gs = torch.tensor([GS], device=cuda)

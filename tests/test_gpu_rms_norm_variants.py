@@ -95,6 +95,8 @@ FORCED = [
     (9, 8192, "cta:vec32:vpt4:tpr128:cluster1:rpc1"),
     (9, 8192, "cta:vec16:vpt4:tpr256:cluster1:rpc1"),
     (9, 8192, "cta:vec8:vpt4:tpr512:cluster1:rpc1"),
+    (5, 16384, "cluster:vec32:vpt1:tpr512:cluster2:rpc1"),
+    (3, 24576, "cluster:vec32:vpt1:tpr768:cluster2:rpc1"),
     (5, 16384, "cluster:vec32:vpt2:tpr256:cluster2:rpc1"),
     (5, 16384, "cluster:vec32:vpt4:tpr64:cluster4:rpc1"),
     (3, 32768, "cluster:vec32:vpt2:tpr128:cluster8:rpc1"),
