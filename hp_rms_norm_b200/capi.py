@@ -51,6 +51,7 @@ EXPORTED = (
     "hprn_set_plan_override",
     "hprn_wait_timeouts",
     "hprn_rms_norm_fp8_group",
+    "hprn_test_stall_bulk_copy",
 )
 
 
@@ -103,6 +104,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
     lib.hprn_set_plan_override.restype = c_int
     lib.hprn_wait_timeouts.argtypes = [ctypes.POINTER(ctypes.c_uint), c_int]
     lib.hprn_wait_timeouts.restype = c_int
+    lib.hprn_test_stall_bulk_copy.argtypes = [i64, ctypes.c_uint64]
+    lib.hprn_test_stall_bulk_copy.restype = c_int
     lib.hprn_rms_norm_fp8_group.argtypes = [vp, vp, i64, i64, vp, vp, vp, i64, i64, i64, i64, i64,
                                             ctypes.c_double, c_int, c_int, c_int, vp, u32]
     lib.hprn_rms_norm_fp8_group.restype = c_int
@@ -202,6 +205,12 @@ def wait_timeouts(reset: bool = False) -> int:
     n = ctypes.c_uint(0)
     _check(load().hprn_wait_timeouts(ctypes.byref(n), 1 if reset else 0))
     return int(n.value)
+
+
+def test_stall_bulk_copy(row: int | None, wait_limit_ns: int = 0) -> None:
+    """Test hook (hprn_test_stall_bulk_copy): later TMA-staged launches make the
+    staged copy of `row` stall so its bounded wait runs out; None turns it off."""
+    _check(load().hprn_test_stall_bulk_copy(-1 if row is None else row, wait_limit_ns))
 
 
 def version() -> int:

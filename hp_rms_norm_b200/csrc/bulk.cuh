@@ -75,15 +75,24 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Waits for phase `parity` of `bar` to complete; false if it did not within
-// kWaitLimitNs (or kWaitMaxPolls polls).
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// `limit_ns` of global time (or kWaitMaxPolls polls).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 0; i < kWaitMaxPolls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - t0 > kWaitLimitNs) break;
+    if (global_ns() - t0 > limit_ns) break;
   }
   return false;
+}
+
+// Counts `bytes` of the current phase's expected transactions as done, as a
+// copy's completion would.  Only the test hook that stalls a staged row uses
+// it: to release the bytes that row's phase expected beyond its copies.
+__device__ __forceinline__ void mbar_complete_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
 }
 
 }  // namespace hprn

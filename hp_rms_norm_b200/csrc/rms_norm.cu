@@ -74,6 +74,9 @@ bool vpt_supported(Kind k, int vec, int vpt, const Variant& v) {
     case kCtaRows:
     case kClusterRows:
       if (vec == 32) return vpt == 1 || vpt == 2 || vpt == 3 || vpt == 4 || vpt == 6 || vpt == 8;
+      // Eight 4-byte vectors per thread in a cluster CTA is not compiled:
+      // ptxas gives that one instance a 4-byte spill (at 48 registers).
+      if (vec == 4 && k == kClusterRows) return vpt == 1 || vpt == 2 || vpt == 4;
       return vpt == 1 || vpt == 2 || vpt == 4 || vpt == 8;
     default: return true;
   }
@@ -250,6 +253,12 @@ Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
 
 bool parse_plan(const std::string& s, Plan* p);
 
+// Test hook of the TMA-staged kernel (hprn_test_stall_bulk_copy): the row of
+// each later call whose staged copy is made to stall (-1: none), and the
+// per-row wait limit in nanoseconds.
+std::atomic<int64_t> g_stall_row{-1};
+std::atomic<uint64_t> g_stall_wait_ns{kWaitLimitNs};
+
 // Optional plan override for benchmarking and tuning: hprn_set_plan_override,
 // or the HP_RMS_NORM_PLAN environment variable (read at the first call).
 // Parsed once when set; calls read it under a mutex only while one is set.
@@ -386,7 +395,9 @@ KernelFn pick_cta(int vpt) {
         case 6: return rms_norm_cta_rows<T, VEC, 6, CL, RES, OUT>;
       }
     }
-    if (vpt == 8) return rms_norm_cta_rows<T, VEC, 8, CL, RES, OUT>;
+    if constexpr (!(CL && VEC == 4)) {
+      if (vpt == 8) return rms_norm_cta_rows<T, VEC, 8, CL, RES, OUT>;
+    }
   }
   switch (vpt) {
     case 1: return rms_norm_cta_rows<T, VEC, 1, CL, RES, OUT>;
@@ -668,6 +679,8 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   a.group_vecs = q.out_form == kOutFp8Group ? q.group_size / epv : 1;
   a.scale_pow2 = q.scale_pow2 != 0;
   a.lanes_per_row = p.kind == kWarpRows ? p.tpr : 32;
+  a.stall_row = g_stall_row.load(std::memory_order_relaxed);
+  a.wait_limit_ns = g_stall_wait_ns.load(std::memory_order_relaxed);
   *plan = p;
   *args = a;
   return HPRN_OK;
@@ -902,6 +915,15 @@ int hprn_wait_timeouts(unsigned int* count, int reset) {
   if (e != cudaSuccess)
     return fail(HPRN_ERR_CUDA, std::string("reading the wait-timeout count: ") + cudaGetErrorString(e));
   *count = v;
+  return ok();
+}
+
+int hprn_test_stall_bulk_copy(int64_t row, uint64_t wait_limit_ns) {
+  using namespace hprn;
+  if (wait_limit_ns > kWaitLimitNs)
+    return fail(HPRN_ERR_INVALID_ARGUMENT, "wait_limit_ns must be at most one second");
+  g_stall_wait_ns.store(wait_limit_ns ? wait_limit_ns : kWaitLimitNs, std::memory_order_relaxed);
+  g_stall_row.store(row < 0 ? -1 : row, std::memory_order_relaxed);
   return ok();
 }
 

@@ -93,6 +93,12 @@ struct RmsArgs {
   int32_t group_vecs;
   int32_t scale_pow2;  // round group scales up to powers of two
   int32_t lanes_per_row;  // warp kind: lanes holding one row (1..32, a power of two)
+  // TMA-staged kernel only: the limit of each per-row mbarrier wait, and a
+  // row (of this call, -1: none) whose staged copy is made to expect
+  // kStallBytes more than it delivers, so that its wait runs out (a test hook:
+  // hprn_test_stall_bulk_copy).
+  int64_t stall_row;
+  uint64_t wait_limit_ns;
 };
 
 // Element pairs go through Blackwell's packed fp32 instructions
@@ -762,7 +768,13 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
 // with the row `stages` ahead.  The weight stays in registers for every row.
 // A wait that gives up (a copy that never completed) ends the CTA after the
 // copies it still has in flight have landed, and counts in g_wait_timeouts.
+// The residual and the output of a row are stored only after every thread's
+// wait for it succeeded, so a CTA that gives up leaves the row it gave up on,
+// and every later row of its share, untouched (input and residual as they
+// were); rows it finished before are complete.
 constexpr int kTmaMaxStages = 16;
+// Bytes a stalled row's phase expects beyond its copies (test hook).
+constexpr uint32_t kStallBytes = 16;
 // Shared memory per CTA kept out of the dynamic ring: the mbarriers and the
 // reduction partials (384 bytes), rounded up.
 constexpr int kTmaStaticSmemReserve = 1024;
@@ -808,7 +820,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_
     const int64_t row = first + k * step;
     const uint32_t bar = smem_u32(&full[s]);
     const uint32_t dst = smem_u32(stage_mem + static_cast<size_t>(s) * stage_bytes);
-    mbar_arrive_expect_tx(bar, stage_bytes);
+    mbar_arrive_expect_tx(bar, stage_bytes + (row == a.stall_row ? kStallBytes : 0u));
     bulk_load(dst, a.x + row * a.x_stride, row_bytes, bar, pol_stream);
     if constexpr (RES) bulk_load(dst + row_bytes, a.r + row * a.r_stride, row_bytes, bar, pol_stream);
   };
@@ -831,7 +843,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_
   uint32_t parity = 0;
   for (int64_t k = 0; k < count; ++k) {
     const int64_t row = first + k * step;
-    const bool arrived = mbar_wait_bounded(smem_u32(&full[s]), parity);
+    const bool arrived = mbar_wait_bounded(smem_u32(&full[s]), parity, a.wait_limit_ns);
     const unsigned char* xs = stage_mem + static_cast<size_t>(s) * stage_bytes;
     uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
     Vec<VEC> xv[VPT];
@@ -844,7 +856,6 @@ __global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_
           xv[j] = ld_staged<VEC>(xs, v);
           if constexpr (RES) {
             add_round<T, VEC>(xv[j], ld_staged<VEC>(xs + row_bytes, v), a0, a1);
-            st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
           } else {
             square_sum<T, VEC>(xv[j], a0, a1);
           }
@@ -856,16 +867,27 @@ __global__ void __launch_bounds__(cta_max_threads(VPT * VEC / 16)) rms_norm_tma_
     // Every thread has read stage s (or some thread gave up waiting).
     if (__syncthreads_or(!arrived)) {
       if (tid == 0) {
-        // Let this CTA's copies still in flight land before its shared memory goes.
+        // Let this CTA's copies still in flight land before its shared memory
+        // goes: wait (bounded) for every stage it issued and has not consumed.
+        // A stalled row's phase is first given the bytes it was made to
+        // expect beyond its copies, so it completes when they have landed.
         int ws = s;
         uint32_t wp = parity;
         for (int64_t j = k; j < count && j < k + stages; ++j) {
+          if (first + j * step == a.stall_row) mbar_complete_tx(smem_u32(&full[ws]), kStallBytes);
           mbar_wait_bounded(smem_u32(&full[ws]), wp);
           if (++ws == stages) ws = 0, wp ^= 1u;
         }
         atomicAdd(&g_wait_timeouts, 1u);
       }
       return;
+    }
+    if constexpr (RES) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = tid + j * nthreads;
+        if (v < a.nvec) st_global<VEC>(rr + static_cast<int64_t>(v) * EPV, xv[j]);
+      }
     }
     if (tid == 0 && k + stages < count) {
       fence_proxy_async_smem();

@@ -256,7 +256,7 @@ void rms_norm_nvfp4(at::Tensor& out, at::Tensor& block_scales, const at::Tensor&
     rows_of(*residual, "residual", &rrows, &rs);
     rp = residual->data_ptr();
   }
-  if (rows == 0) return;
+  if (rows == 0 || hidden == 0) return;
   const c10::cuda::CUDAGuard guard(input.device());
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(input.device().index()).stream();
   check_status(hprn_rms_norm_nvfp4(out.data_ptr(), static_cast<uint8_t*>(block_scales.data_ptr()),

@@ -225,6 +225,9 @@ HPRN_API int hprn_version(void);
  * row (1..32, a power of two); C CTAs per row; R rows per CTA, or for kind tma
  * the depth of the CTA's ring of TMA-staged rows) and returns HPRN_OK.  Performs no launch.  Null input/residual pointers plan for
  * 256-byte-aligned tensors; without a usable device it plans for a 148-SM B200.
+ * The weight is assumed to be aligned like the input: a call whose weight is
+ * less aligned than its input gets a narrower vector width (and so possibly
+ * another plan) than the one returned here.
  */
 HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const void* input,
                                 const void* residual, int64_t input_row_stride,
@@ -243,14 +246,33 @@ HPRN_API int hprn_set_plan_override(const char* plan);
 
 /*
  * No reference counterpart.  Kernels that stage rows through TMA bulk copies
- * wait on mbarriers with a bound (one second); a CTA that gives up a wait
- * leaves its remaining rows unwritten and counts itself here, on its device.
+ * (plan kind tma, reached only through a plan override) wait on mbarriers with
+ * a bound (one second); a CTA that gives up a wait leaves the row it gave up
+ * on and its remaining rows untouched (input and residual as they were) and
+ * counts itself here, on its device.  The call that launched it still returns
+ * HPRN_OK: a caller that forces a tma plan must read this count.
  * Writes the current device's count into *count and, if `reset` is non-zero,
  * clears it.  Synchronous; synchronise the streams that launched the kernels
  * first.  A non-zero count means the launches since the last reset produced
  * incomplete results.
  */
 HPRN_API int hprn_wait_timeouts(unsigned int* count, int reset);
+
+/*
+ * No reference counterpart.  Test hook for the bounded waits above: every
+ * later launch of a TMA-staged plan in this process makes the staged copy of
+ * row `row` (counted from the first row of that call; -1 turns the hook off)
+ * expect 16 bytes more than its copies deliver, so the row's mbarrier phase
+ * cannot complete and its wait runs out after `wait_limit_ns` nanoseconds
+ * (at most one second; 0 keeps the built-in one second).  The CTA holding
+ * that row then takes its give-up path: it waits for the copies it still has
+ * in flight (releasing the stalled row's 16 extra bytes itself, so that wait
+ * ends once its copies have landed), leaves that row and its later rows
+ * untouched, and counts itself in hprn_wait_timeouts.  No fault and no hang:
+ * every wait stays bounded.  Plans of other kinds ignore it.  Process-global;
+ * for tests only.
+ */
+HPRN_API int hprn_test_stall_bulk_copy(int64_t row, uint64_t wait_limit_ns);
 
 #ifdef __cplusplus
 }

@@ -181,3 +181,12 @@ def test_plan_override_parsing():
 def test_wait_timeouts_needs_a_count_pointer():
     lib = capi.load()
     assert lib.hprn_wait_timeouts(None, 0) == capi.ERR_INVALID_ARGUMENT
+
+
+def test_stall_hook_arguments():
+    """The bounded-wait test hook takes a row (or -1: off) and a limit of at
+    most one second; it only records settings, so it runs without a GPU."""
+    expect_error(lambda: capi.test_stall_bulk_copy(0, 2_000_000_000), capi.ERR_INVALID_ARGUMENT,
+                 "one second")
+    capi.test_stall_bulk_copy(3, 1_000_000)
+    capi.test_stall_bulk_copy(None)

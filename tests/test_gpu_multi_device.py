@@ -78,3 +78,39 @@ def test_rows_sharded_over_devices_match_one_device(two_devices):
     r_cat = torch.cat([p[1].to(two_devices[0]) for p in parts])
     assert torch.equal(x_cat.view(torch.int16), x_one.view(torch.int16))
     assert torch.equal(r_cat.view(torch.int16), r_one.view(torch.int16))
+
+
+def test_rows_sharded_over_ranks_under_torchrun(two_devices, tmp_path):
+    """The same split as above in bench.py's multi-GPU layout: two processes
+    started by torchrun, one per GPU, each running its own block of rows
+    (tests/shard_rank_worker.py).  The blocks put together equal the
+    one-device result bit for bit."""
+    import os
+    import socket
+    import subprocess
+    import sys
+
+    import numpy as np
+
+    from tests import shard_rank_worker as W
+
+    x0, w0, r0, eps = make_inputs(W.ROWS, W.HIDDEN, torch.bfloat16, "c0", seed=W.SEED, device="cpu")
+    x, w, r = x0.to(two_devices[0]), w0.to(two_devices[0]), r0.to(two_devices[0])
+    H.hp_rms_norm(x, w, r, eps)
+    torch.cuda.synchronize(two_devices[0])
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", CUDA_VISIBLE_DEVICES=os.environ.get(
+        "CUDA_VISIBLE_DEVICES", "0,1"))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port),
+           os.path.join(root, "tests", "shard_rank_worker.py"), str(tmp_path)]
+    p = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stderr[-3000:]
+    parts = [np.load(tmp_path / f"rank{k}.npz") for k in range(2)]
+    assert int(parts[0]["start"]) == 0 and int(parts[0]["stop"]) == int(parts[1]["start"])
+    assert int(parts[1]["stop"]) == W.ROWS
+    assert np.array_equal(np.concatenate([q["res"] for q in parts]), bits(r))
+    assert np.array_equal(np.concatenate([q["out"] for q in parts]), bits(x))

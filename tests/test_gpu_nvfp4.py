@@ -134,3 +134,16 @@ def test_nvfp4_argument_errors(cuda):
     w2 = torch.ones(1024, dtype=torch.bfloat16, device=cuda)
     with pytest.raises(RuntimeError, match="32-byte aligned"):
         hp_rms_norm_b200.rms_norm_nvfp4(x2, w2, eps, gs)
+
+
+def test_nvfp4_empty_rows_are_a_no_op(cuda):
+    """[N, 0] and [0, H] inputs return empty outputs without a launch, as the
+    other out-of-place forms do."""
+    gs = torch.tensor([GS], device=cuda)
+    for rows, hidden in ((4, 0), (0, 64)):
+        x = torch.empty(rows, hidden, dtype=torch.bfloat16, device=cuda)
+        w = torch.ones(hidden, dtype=torch.bfloat16, device=cuda)
+        r = torch.empty_like(x)
+        codes, scales = hp_rms_norm_b200.rms_norm_nvfp4(x, w, 1e-6, gs, residual=r)
+        torch.cuda.synchronize()
+        assert codes.shape == (rows, hidden // 2) and scales.shape == (rows, hidden // 16)

@@ -170,3 +170,82 @@ def test_tma_plan_rejections(cuda):
     with forced("tma:vec16:vpt1:tpr128:cluster1:rpc2"):
         with pytest.raises(capi.HprnError, match="vector width"):
             capi.rms_norm_tensors(xb, w[:1024].contiguous(), r[:, :1024].contiguous(), eps)
+
+
+def _row_states(got_x, got_r, x0, r0, want_out, want_res, fused):
+    """Per row: 'done' (residual bit-exact, output within the parity bar),
+    'untouched' (input and residual as they were), or 'mixed'."""
+    states = []
+    for i in range(got_x.shape[0]):
+        untouched = np.array_equal(got_x[i], x0[i]) and (not fused or np.array_equal(got_r[i], r0[i]))
+        res_ok = not fused or np.array_equal(got_r[i], want_res[i])
+        a = got_x[i].astype(np.int32)
+        b = want_out[i].astype(np.int32)
+        oa = np.where(a & 0x8000, -(a & 0x7FFF), a)
+        ob = np.where(b & 0x8000, -(b & 0x7FFF), b)
+        done = res_ok and int(np.abs(oa - ob).max()) <= 1
+        states.append("untouched" if untouched else ("done" if done else "mixed"))
+    return states
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_tma_wait_that_runs_out_is_reported(cuda, fused):
+    """The bounded-wait give-up path, made to run on purpose: the test hook
+    hprn_test_stall_bulk_copy makes one row's staged copy expect 16 bytes more
+    than it delivers, so that row's mbarrier phase cannot complete and its wait
+    runs out after 2 ms.  The call still completes; the CTA holding the row
+    lets its other copies land, counts itself once in hprn_wait_timeouts and
+    returns.  Every row is then either done exactly as the oracle says or
+    untouched, and the untouched rows are exactly the stalled row and the
+    later rows of the same CTA (rows stall, stall + G, ... of the persistent
+    grid of G CTAs).  A second call stalls the second row of a CTA, whose first
+    row must be done.  The counter resets to 0, and a call without the hook
+    matches the oracle."""
+    rows, hidden = 4096, 1024
+    plan = "tma:vec16:vpt1:tpr128:cluster1:rpc4"
+    x0, w, r0, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=77, device=cuda)
+    xb, wb, rb = bits(x0), bits(w), bits(r0)
+    want_out, want_res, _ = O.rms_norm_out(O.BF16, xb, wb, eps, r=rb if fused else None)
+    sentinel = np.full_like(xb, 0x7E7E)
+
+    def stalled_call(stall_row):
+        x, r = x0.clone(), r0.clone()
+        out = x if fused else torch.from_numpy(sentinel.view(np.int16)).to(cuda).view(torch.bfloat16)
+        capi.wait_timeouts(reset=True)
+        try:
+            capi.test_stall_bulk_copy(stall_row, 2_000_000)
+            with forced(plan):
+                if fused:
+                    capi.rms_norm_tensors(x, w, r, eps)
+                else:
+                    capi.rms_norm_out_tensors(out, x, w, None, eps)
+            torch.cuda.synchronize()
+        finally:
+            capi.test_stall_bulk_copy(None)
+        assert capi.wait_timeouts(reset=True) == 1, "exactly one CTA gives up"
+        assert capi.wait_timeouts() == 0, "the count resets"
+        if fused:
+            return _row_states(bits(x), bits(r), xb, rb, want_out, want_res, True)
+        assert torch.equal(x.view(torch.int16), x0.view(torch.int16)), "plain form: input unchanged"
+        return _row_states(bits(out), bits(r), sentinel, rb, want_out, want_res, False)
+
+    states = stalled_call(0)
+    assert "mixed" not in states
+    untouched = [i for i, s in enumerate(states) if s == "untouched"]
+    assert untouched[0] == 0
+    grid = untouched[1] if len(untouched) > 1 else rows
+    assert untouched == list(range(0, rows, grid)), untouched[:8]
+    if grid + 3 < rows:
+        states = stalled_call(grid + 3)
+        assert "mixed" not in states
+        untouched = [i for i, s in enumerate(states) if s == "untouched"]
+        assert untouched == list(range(grid + 3, rows, grid)), untouched[:8]
+        assert states[3] == "done", "the stalled CTA's rows before the stall are complete"
+
+    x, r = x0.clone(), r0.clone()
+    with forced(plan):
+        capi.rms_norm_tensors(x, w, r, eps)
+    torch.cuda.synchronize()
+    want_out_f, want_res_f = O.fused_add_rms_norm(O.BF16, xb, wb, rb, eps, O.SS_UNROUNDED)
+    assert_bits_equal(bits(r), want_res_f, O.BF16, label="after the stall: residual")
+    assert_output_close(bits(x), want_out_f, O.BF16, label="after the stall: output")
