@@ -3,6 +3,7 @@
     python -m hp_rms_norm_b200.tune [--rows 4096] [--hidden 1024,2048,...]
                                     [--dtype bf16|fp16] [--warm] [--json out.json]
                                     [--no-tma | --tma-only] [--isolated] [--copy]
+                                    [--default-only]
                                     [--variant fused|fused_out|plain|fused_fp8s|fused_fp8d|
                                                plain_fp8s|plain_fp8d|fused_nvfp4|plain_nvfp4|
                                                fused_fp8g|plain_fp8g]
@@ -153,7 +154,7 @@ def isolated_us(torch, fn, nsets: int, flush, reps: int = 7) -> float:
 
 def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False,
           variant: str = "fused", tma: bool = True, tma_only: bool = False,
-          isolated: bool = False, copy: bool = False) -> dict:
+          isolated: bool = False, copy: bool = False, default_only: bool = False) -> dict:
     import torch
 
     from . import capi
@@ -209,8 +210,9 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
 
         timings = {}
         try:
-            plans = candidates(h // 16, variant == "fused") if h % 16 == 0 else []
-            if form == capi.OUT_SAME and (tma or tma_only) and h % 8 == 0:
+            plans = candidates(h // 16, variant == "fused") if h % 16 == 0 and not default_only \
+                else []
+            if form == capi.OUT_SAME and (tma or tma_only) and h % 8 == 0 and not default_only:
                 plans = (plans if not tma_only else []) + tma_candidates(h, res_needed)
             for p in plans:
                 capi.set_plan_override(p)
@@ -259,9 +261,12 @@ def main() -> None:
                     help="time single launches after an L2 flush instead of back-to-back graphs")
     ap.add_argument("--copy", action="store_true",
                     help="also time torch's copy_ of the same bytes, the same way")
+    ap.add_argument("--default-only", action="store_true",
+                    help="time only the built-in heuristic's plan (e.g. under an ncu capture)")
     a = ap.parse_args()
     res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm, a.variant,
-                tma=not a.no_tma, tma_only=a.tma_only, isolated=a.isolated, copy=a.copy)
+                tma=not a.no_tma, tma_only=a.tma_only, isolated=a.isolated, copy=a.copy,
+                default_only=a.default_only)
     print(f"{'hidden':>7} {'default plan':40} {'us':>8} {'GB/s':>8}   {'best plan':40} {'us':>8}"
           + (f" {'copy us':>8} {'copy GB/s':>9}" if a.copy else ""))
     for h, r in res.items():
