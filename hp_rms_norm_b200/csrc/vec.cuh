@@ -194,6 +194,38 @@ __device__ __forceinline__ Vec<2> ld_l2<2>(const void* p) {
   return v;
 }
 
+// The same .cg load with an L2 cache policy (the two-pass kernel's last read
+// of a row it staged in L2: evict_first).  Vector widths below 8 bytes take
+// the plain load.
+template <int VEC>
+__device__ __forceinline__ Vec<VEC> ld_l2_hint(const void* p, uint64_t pol) {
+  if constexpr (VEC == 32) {
+    Vec<32> v;
+    asm volatile("ld.global.cg.L2::cache_hint.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8], %9;"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]),
+                   "=r"(v.w[5]), "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p), "l"(pol)
+                 : "memory");
+    return v;
+  } else if constexpr (VEC == 16) {
+    Vec<16> v;
+    asm volatile("ld.global.cg.L2::cache_hint.v4.b32 {%0,%1,%2,%3}, [%4], %5;"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+                 : "l"(p), "l"(pol)
+                 : "memory");
+    return v;
+  } else if constexpr (VEC == 8) {
+    Vec<8> v;
+    asm volatile("ld.global.cg.L2::cache_hint.v2.b32 {%0,%1}, [%2], %3;"
+                 : "=r"(v.w[0]), "=r"(v.w[1])
+                 : "l"(p), "l"(pol)
+                 : "memory");
+    return v;
+  } else {
+    return ld_l2<VEC>(p);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Stores.
 template <int VEC>
@@ -227,6 +259,29 @@ __device__ __forceinline__ void st_global<4>(void* p, const Vec<4>& v) {
 template <>
 __device__ __forceinline__ void st_global<2>(void* p, const Vec<2>& v) {
   asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(v.h) : "memory");
+}
+
+// A store with an L2 cache policy (the two-pass kernel's rounded residual,
+// which its second pass reads back: evict_last keeps it in L2 ahead of the
+// streamed rows).  Vector widths below 8 bytes take the plain store.
+template <int VEC>
+__device__ __forceinline__ void st_global_hint(void* p, const Vec<VEC>& v, uint64_t pol) {
+  if constexpr (VEC == 32) {
+    asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8}, %9;" ::"l"(p),
+                 "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]),
+                 "r"(v.w[6]), "r"(v.w[7]), "l"(pol)
+                 : "memory");
+  } else if constexpr (VEC == 16) {
+    asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.w[0]),
+                 "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "l"(pol)
+                 : "memory");
+  } else if constexpr (VEC == 8) {
+    asm volatile("st.global.L2::cache_hint.v2.b32 [%0], {%1,%2}, %3;" ::"l"(p), "r"(v.w[0]),
+                 "r"(v.w[1]), "l"(pol)
+                 : "memory");
+  } else {
+    st_global<VEC>(p, v);
+  }
 }
 
 // ---------------------------------------------------------------------------
