@@ -242,16 +242,9 @@ __device__ __forceinline__ Vec<8> quantize_nvfp4(const Vec<32>& rv, const Vec<32
   const float2 qs2 = make_float2(qs, qs);
   Vec<8> o;
 #pragma unroll
-  for (int w = 0; w < 2; ++w) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const __nv_fp4x2_storage_t p =
-          __nv_cvt_float2_to_fp4x2(__fmul2_rn(y[4 * w + b], qs2), __NV_E2M1, cudaRoundNearest);
-      word |= static_cast<uint32_t>(p) << (8 * b);
-    }
-    o.w[w] = word;
-  }
+  for (int w = 0; w < 2; ++w)
+    o.w[w] = e2m1x8(__fmul2_rn(y[4 * w], qs2), __fmul2_rn(y[4 * w + 1], qs2),
+                    __fmul2_rn(y[4 * w + 2], qs2), __fmul2_rn(y[4 * w + 3], qs2));
   *sf_out = sf;
   return o;
 }

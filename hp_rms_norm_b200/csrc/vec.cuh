@@ -381,6 +381,27 @@ __device__ __forceinline__ uint16_t pack1<__half>(float f) {
 }
 
 // ---------------------------------------------------------------------------
+// Eight e2m1 (NVFP4) codes of four fp32 pairs, converted and packed in
+// registers: four cvt.rn.satfinite.e2m1x2.f32 assembled into one 32-bit word
+// by a mov of the bytes, element order preserved (the first element in the
+// lowest nibble).  The conversion is the one cuda_fp4.h uses: round to
+// nearest even, saturating to the largest finite value.  Against the
+// intrinsic's byte-by-byte shifts and ORs: 10.0 instead of 10.9 instructions
+// per element for plain RMSNorm with NVFP4 output (4096 x 8192).
+__device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 d) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y), "f"(d.x), "f"(d.y));
+  return r;
+}
+
+// ---------------------------------------------------------------------------
 // Programmatic dependent launch.  pdl_wait() at kernel entry, before the
 // first global-memory access: blocks until the grid this one depends on (if it
 // was launched that way) has completed and its memory is visible.

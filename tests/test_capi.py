@@ -60,6 +60,22 @@ def test_plan_is_for_the_fused_form_whatever_the_pointers():
     assert capi.plan(4096, 1536) == "warp:vec32:vpt3:tpr32:cluster1:rpc4"
 
 
+@pytest.mark.parametrize("rows,hidden,plan", [
+    (1, 1024, "cta:vec16:vpt1:tpr128:cluster1:rpc1"),
+    (512, 1024, "cta:vec16:vpt1:tpr128:cluster1:rpc1"),
+    (33, 1536, "cta:vec16:vpt1:tpr192:cluster1:rpc1"),
+    (128, 2048, "cta:vec16:vpt1:tpr256:cluster1:rpc1"),
+    (513, 1024, "warp:vec32:vpt2:tpr32:cluster1:rpc4"),
+    (512, 512, "warp:vec32:vpt1:tpr32:cluster1:rpc4"),
+    (512, 4096, "cta:vec32:vpt1:tpr256:cluster1:rpc1"),
+])
+def test_small_batch_plans(rows, hidden, plan):
+    """Decode-sized batches of fused rows of 528-2048 elements take one CTA per
+    row at 16-byte vectors; larger batches, shorter rows and longer rows keep
+    their own rules."""
+    assert capi.plan(rows, hidden) == plan
+
+
 @pytest.mark.parametrize("hidden,plan", [
     # rows past one CTA: eight-CTA clusters, one vector per thread up to 512
     # vectors per CTA, else two (the long-row sweep's fit)

@@ -62,6 +62,18 @@ SWEEP = list(range(1024, 16384 + 1, 1024)) + [20480, 24576, 28672, 32768]
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("rows,hidden", [(r, h) for r in (1, 7, 33, 128, 512, 513)
+                                         for h in (1024, 1536, 2048)])
+def test_small_batch_short_rows(cuda, dtype, rows, hidden):
+    """Decode-sized batches of rows of 1024-2048 elements, config-2
+    distributions: one CTA per row at 16-byte vectors up to 512 rows, the warp
+    and CTA rules from 513."""
+    tdtype, code = DTYPES[dtype]
+    x, w, r, eps = make_inputs(rows, hidden, tdtype, "c2", seed=rows * 11 + hidden, device=cuda)
+    check_vs_oracle(x, w, r, eps, code, f"{dtype} {rows}x{hidden} {capi.plan(rows, hidden)}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 @pytest.mark.parametrize("hidden", SWEEP)
 def test_hidden_sweep_vs_oracle(cuda, dtype, hidden):
     tdtype, code = DTYPES[dtype]
