@@ -87,6 +87,7 @@ struct ActArgs {
   int64_t chunks_per_row;  // CTAs per row
   int64_t out_stride;      // elements
   int64_t in_stride;
+  int64_t prefetch_ctas;   // CTAs blockIdx.x < this (the first wave) prefetch into L2
 };
 
 template <typename T, int VEC, int U, int ACT>
@@ -99,6 +100,13 @@ __global__ void __launch_bounds__(256) act_and_mul_rows(ActArgs a) {
   uint16_t* dst = a.out + row * a.out_stride;
   const uint64_t pol = policy_evict_first();
   const int64_t base = chunk * (static_cast<int64_t>(blockDim.x) * U) + threadIdx.x;
+  const int64_t first = base - threadIdx.x;  // the CTA's first vector
+  if (threadIdx.x == 0 && first < a.nvec && blockIdx.x < a.prefetch_ctas) {
+    const uint64_t bytes =
+        static_cast<uint64_t>(min(static_cast<int64_t>(blockDim.x) * U, a.nvec - first)) * VEC;
+    prefetch_l2(gate + first * EPV, bytes);
+    prefetch_l2(up + first * EPV, bytes);
+  }
   pdl_wait();
 
   Vec<VEC> g[U], u[U];
@@ -199,6 +207,7 @@ int hprn_act_and_mul(void* out, const void* input, int64_t rows, int64_t d,
   const int64_t grid = rows * a.chunks_per_row;
   if (grid > 2147483647LL) return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor too large for one launch");
   ActFn fn = dtype == HPRN_DTYPE_BF16 ? pick_act<__nv_bfloat16>(act, vec) : pick_act<__half>(act, vec);
+  a.prefetch_ctas = first_wave_ctas(dev, reinterpret_cast<const void*>(fn), kActThreads);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);

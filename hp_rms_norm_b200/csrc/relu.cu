@@ -59,6 +59,7 @@ struct ReluArgs {
   int64_t chunks_per_row;  // CTAs per row
   int64_t out_stride;      // elements
   int64_t in_stride;
+  int64_t prefetch_ctas;   // CTAs blockIdx.x < this (the first wave) prefetch into L2
   int64_t tail_begin;      // flat mode: first element not covered by vectors
   int64_t tail_end;
 };
@@ -72,6 +73,10 @@ __global__ void __launch_bounds__(256) relu_rows(ReluArgs a) {
   uint16_t* dst = a.out + row * a.out_stride;
   const uint64_t pol = policy_evict_first();
   const int64_t base = chunk * (static_cast<int64_t>(blockDim.x) * U) + threadIdx.x;
+  const int64_t first = base - threadIdx.x;  // the CTA's first vector
+  if (threadIdx.x == 0 && first < a.nvec && blockIdx.x < a.prefetch_ctas)
+    prefetch_l2(src + first * EPV,
+                static_cast<uint64_t>(min(static_cast<int64_t>(blockDim.x) * U, a.nvec - first)) * VEC);
   pdl_wait();
 
   Vec<VEC> v[U];
@@ -184,6 +189,7 @@ int hprn_relu_ex(void* out, const void* input, int64_t rows, int64_t hidden,
   const int64_t grid = a.rows * a.chunks_per_row;
   if (grid > 2147483647LL) return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor too large for one launch");
   ReluFn fn = dtype == HPRN_DTYPE_BF16 ? pick_relu<__nv_bfloat16>(vec) : pick_relu<__half>(vec);
+  a.prefetch_ctas = first_wave_ctas(dev, reinterpret_cast<const void*>(fn), kReluThreads);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);

@@ -28,7 +28,15 @@ struct Plan {
   int tpr = 32;          // threads per CTA working on one row slice
   int cluster = 1;       // CTAs per row
   int rows_per_cta = 1;  // warp kind: rows per CTA; tma kind: ring depth (rows in flight per CTA)
+  // Launch knobs (-1: the default for the plan, see default_knobs):
+  int prefetch = -1;  // L2 prefetch before the programmatic-launch wait: 0 none,
+                      // 1 the grid's first wave of CTAs, 2 every CTA
+  int early = -1;     // 1: trigger dependents after the row reduction, 0: after the last store
+  bool knobs_given = false;  // set by parse_plan when the string carried both knobs
+  bool knobs_only = false;   // override "default:pf<p>:et<e>": the default plan, these knobs
 };
+
+enum Prefetch { kPrefetchNone = 0, kPrefetchFirstWave = 1, kPrefetchAll = 2 };
 
 // Kernel family of one call: residual or not, and the output form.
 struct Variant {
@@ -51,8 +59,11 @@ const char* kind_name(Kind k) {
 
 std::string plan_string(const Plan& p) {
   char buf[96];
-  snprintf(buf, sizeof(buf), "%s:vec%d:vpt%d:tpr%d:cluster%d:rpc%d", kind_name(p.kind), p.vec,
-           p.vpt, p.tpr, p.cluster, p.rows_per_cta);
+  int n = snprintf(buf, sizeof(buf), "%s:vec%d:vpt%d:tpr%d:cluster%d:rpc%d", kind_name(p.kind),
+                   p.vec, p.vpt, p.tpr, p.cluster, p.rows_per_cta);
+  // Knobs given explicitly (a plan override) are echoed; defaults are implied.
+  if (p.knobs_given && n > 0 && n < static_cast<int>(sizeof(buf)))
+    snprintf(buf + n, sizeof(buf) - n, ":pf%d:et%d", p.prefetch, p.early);
   return buf;
 }
 
@@ -265,6 +276,41 @@ Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
   return p;
 }
 
+// Fills the launch knobs a plan leaves at -1 (default_plan's plans, and
+// overrides without ":pf..:et.."), from cold-L2 timings of every combination
+// (tune.py --knobs: one process per combination, three runs each) at batch
+// 4096 x hidden 1024-32768 for the 16-bit, NVFP4, dynamic and per-group fp8
+// forms, and at 64 rows x hidden 4096-1M (cluster and two-pass kernels):
+//   * triggering dependents after the row reduction is as fast or faster
+//     everywhere (4096 x 1024: fused 6.07 vs 6.12 us, plain NVFP4 3.75 vs
+//     4.14, fused per-group fp8 6.29 vs 6.80; 64 x 262144: 24.8 vs 25.4);
+//   * the L2 prefetch pays in every CTA while one CTA prefetches less than
+//     64 KB (fused 4096 x 1024 / 4096: 6.07 / 21.1 us, against 6.38 / 21.5
+//     without it; at 4096 x 4096 about half of the gain comes from the first
+//     wave alone);
+//   * past that, and from 64 KB for the fused 16-bit form, it pays in the
+//     first wave only (4096 x 32768 fused: 157.6 us, 159.3 with every CTA,
+//     157.8 with none; 4096 x 16384: 79.9 against 80.4 with every CTA), and
+//     so it does for the plain NVFP4 and dynamic or per-group fp8 forms at
+//     four vectors per thread (plain NVFP4 at 4096 x 32768: 60.4 vs 63.5).
+void default_knobs(Plan* p, const Variant& var) {
+  if (p->kind == kTma) {  // the TMA-staged kernel stages rows itself and triggers at its end
+    p->prefetch = kPrefetchNone;
+    p->early = 0;
+    return;
+  }
+  if (p->early < 0) p->early = 1;
+  if (p->prefetch < 0) {
+    const int threads = p->kind == kWarpRows ? p->rows_per_cta * p->tpr : p->tpr;
+    const int vpt = p->kind == kTwoPass ? kTwoPassUnroll : p->vpt;  // two passes: its first chunk
+    const int64_t bytes = static_cast<int64_t>(threads) * vpt * p->vec * (var.res ? 2 : 1);
+    const bool issue_bound_plain =
+        !var.res && var.out != kOutSame && var.out != kOutFp8Static && p->vpt >= 4;
+    const bool big = bytes > 65536 || (bytes == 65536 && var.full());
+    p->prefetch = (big || issue_bound_plain) ? kPrefetchFirstWave : kPrefetchAll;
+  }
+}
+
 bool parse_plan(const std::string& s, Plan* p);
 
 // Test hook of the TMA-staged kernel (hprn_test_stall_bulk_copy): the row of
@@ -301,11 +347,26 @@ bool override_plan(Plan* out) {
 }
 
 bool parse_plan(const std::string& s, Plan* p) {
+  if (s.rfind("default:", 0) == 0) {
+    int pf = -1, et = -1, end = 0;
+    if (sscanf(s.c_str(), "default:pf%d:et%d%n", &pf, &et, &end) != 2 ||
+        static_cast<size_t>(end) != s.size() || pf < 0 || pf > 2 || et < 0 || et > 1)
+      return false;
+    p->prefetch = pf;
+    p->early = et;
+    p->knobs_given = p->knobs_only = true;
+    return true;
+  }
   char kind[16] = {0};
-  int vec, vpt, tpr, cluster, rpc;
-  if (sscanf(s.c_str(), "%15[a-z]:vec%d:vpt%d:tpr%d:cluster%d:rpc%d", kind, &vec, &vpt, &tpr,
-             &cluster, &rpc) != 6)
-    return false;
+  int vec, vpt, tpr, cluster, rpc, pf = -1, et = -1, end = 0;
+  const int got = sscanf(s.c_str(), "%15[a-z]:vec%d:vpt%d:tpr%d:cluster%d:rpc%d%n:pf%d:et%d%n",
+                         kind, &vec, &vpt, &tpr, &cluster, &rpc, &end, &pf, &et, &end);
+  // Six fields, optionally followed by both knobs (":pf<0|1|2>:et<0|1>"), and nothing else.
+  if ((got != 6 && got != 8) || static_cast<size_t>(end) != s.size()) return false;
+  if (got == 8 && (pf < 0 || pf > 2 || et < 0 || et > 1)) return false;
+  p->prefetch = got == 8 ? pf : -1;
+  p->early = got == 8 ? et : -1;
+  p->knobs_given = got == 8;
   std::string k(kind);
   if (k == "warp") p->kind = kWarpRows;
   else if (k == "cta") p->kind = kCtaRows;
@@ -661,7 +722,12 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
     return fail(HPRN_ERR_INVALID_ARGUMENT, "rows longer than 16384 vectors are supported with a "
                                            "16-bit output only");
   Plan o;
-  if (override_plan(&o)) {
+  const bool overridden = override_plan(&o);
+  if (overridden && o.knobs_only) {
+    p.prefetch = o.prefetch;
+    p.early = o.early;
+    p.knobs_given = true;
+  } else if (overridden) {
     std::string why;
     if (o.vec > max_vec || q.hidden % (o.vec / 2) != 0)
       return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override vector width not allowed here");
@@ -670,6 +736,7 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
       return fail(HPRN_ERR_INVALID_ARGUMENT, "plan override rejected: " + why);
     p = o;
   }
+  default_knobs(&p, var);
   const int epv = p.vec / 2;
   RmsArgs a;
   a.x = static_cast<const uint16_t*>(q.x);
@@ -695,6 +762,8 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   a.lanes_per_row = p.kind == kWarpRows ? p.tpr : 32;
   a.stall_row = g_stall_row.load(std::memory_order_relaxed);
   a.wait_limit_ns = g_stall_wait_ns.load(std::memory_order_relaxed);
+  a.prefetch_ctas = 0;  // set per launch
+  a.early_trigger = p.early;
   *plan = p;
   *args = a;
   return HPRN_OK;
@@ -770,6 +839,11 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
   const bool clustered = p.kind == kClusterRows || (p.kind == kTwoPass && p.cluster > 1);
   const int64_t ctas_per_unit = clustered ? p.cluster : 1;
   const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
+  const int threads = p.kind == kWarpRows ? p.rows_per_cta * p.tpr : p.tpr;
+  a.prefetch_ctas = p.prefetch == kPrefetchNone ? 0
+                    : p.prefetch == kPrefetchAll
+                        ? INT64_MAX
+                        : first_wave_ctas(dev, reinterpret_cast<const void*>(fn), threads);
 
   int64_t done = 0;
   while (done < a.rows) {
@@ -788,7 +862,7 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(static_cast<unsigned>(units * ctas_per_unit), 1, 1);
-    cfg.blockDim = dim3(p.kind == kWarpRows ? p.rows_per_cta * p.tpr : p.tpr, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
     cfg.attrs = attr;

@@ -99,6 +99,12 @@ struct RmsArgs {
   // hprn_test_stall_bulk_copy).
   int64_t stall_row;
   uint64_t wait_limit_ns;
+  // CTAs blockIdx.x < prefetch_ctas prefetch their first rows into L2 before
+  // the programmatic-launch wait (0: none; the grid's first wave; or all).
+  int64_t prefetch_ctas;
+  // Nonzero: trigger dependents (pdl_trigger) right after the row reduction
+  // instead of after the last store.
+  int32_t early_trigger;
 };
 
 // Element pairs go through Blackwell's packed fp32 instructions
@@ -426,9 +432,13 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   const int sub = threadIdx.x & (lpr - 1);
   const int64_t row = static_cast<int64_t>(blockIdx.x) * a.rows_per_cta + threadIdx.x / lpr;
   const bool active = row < a.rows;
-  pdl_wait();
   const uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
+  if (active && sub == 0 && blockIdx.x < a.prefetch_ctas) {
+    prefetch_l2(xr, static_cast<uint64_t>(a.nvec) * VEC);
+    if constexpr (RES) prefetch_l2(rr, static_cast<uint64_t>(a.nvec) * VEC);
+  }
+  pdl_wait();
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
 
@@ -479,6 +489,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
     }
   }
   const float inv = rsqrtf(fmaf(lane_group_sum(a0 + a1, lpr), a.inv_hidden, a.eps));
+  if (a.early_trigger) pdl_trigger();
   float inv_scale = static_inv_scale<OUT>(a);
   if constexpr (OUT == kOutFp8Dynamic) {
     const float scale = fmaxf(lane_group_max(m, lpr) * inv, kMinAmax) / kE4m3Max;
@@ -497,7 +508,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
                              inv_scale);
     }
   }
-  pdl_trigger();
+  if (!a.early_trigger) pdl_trigger();
 }
 
 // Largest CTA a cta/cluster kernel with VPT vectors per thread is compiled
@@ -540,11 +551,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
   int64_t row;
   int v_begin = 0, v_end = a.nvec;
   uint32_t crank = 0, csize = 1;
-  pdl_wait();
   if constexpr (CLUSTER) {
-    // Phase 1 of the cluster barrier: completes once every CTA of the cluster
-    // is running, which makes their shared memory safe to write.
-    cluster_arrive_relaxed();
     crank = cluster_ctarank();
     csize = cluster_nctarank();
     row = cluster_id_x();
@@ -555,6 +562,15 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
   }
   const uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
+  if (tid == 0 && v_end > v_begin && blockIdx.x < a.prefetch_ctas) {
+    const uint64_t bytes = static_cast<uint64_t>(v_end - v_begin) * VEC;
+    prefetch_l2(xr + static_cast<int64_t>(v_begin) * EPV, bytes);
+    if constexpr (RES) prefetch_l2(rr + static_cast<int64_t>(v_begin) * EPV, bytes);
+  }
+  pdl_wait();
+  // Phase 1 of the cluster barrier: completes once every CTA of the cluster
+  // is running, which makes their shared memory safe to write.
+  if constexpr (CLUSTER) cluster_arrive_relaxed();
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
 
@@ -625,7 +641,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
     if constexpr (kAmax) amax = warp_max(lane < static_cast<int>(csize) ? cta_amax[lane] : 0.f);
   }
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
-
+  if (a.early_trigger) pdl_trigger();
   float inv_scale = static_inv_scale<OUT>(a);
   if constexpr (kAmax) {
     const float scale = fmaxf(amax * inv, kMinAmax) / kE4m3Max;
@@ -644,7 +660,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
                              inv_scale);
     }
   }
-  pdl_trigger();
+  if (!a.early_trigger) pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------
@@ -661,11 +677,13 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
 // row); each CTA pushes its partial sum into every peer's shared memory, and
 // one cluster barrier completes the row's sum between the passes.
 constexpr int kTwoPassThreads = 512;
+// Vectors each thread has in flight per chunk of a two-pass row.
+constexpr int kTwoPassUnroll = 4;
 
 template <typename T, int VEC, bool RES, bool CLUSTER>
 __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
-  constexpr int U = 4;
+  constexpr int U = kTwoPassUnroll;
   __shared__ float warp_part[32];
   __shared__ float cta_part[8];
   const int tid = threadIdx.x;
@@ -675,9 +693,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   int64_t row;
   int v_begin = 0, v_end = a.nvec;
   uint32_t crank = 0, csize = 1;
-  pdl_wait();
   if constexpr (CLUSTER) {
-    cluster_arrive_relaxed();  // phase 1: completes once every peer is running
     crank = cluster_ctarank();
     csize = cluster_nctarank();
     row = cluster_id_x();
@@ -689,6 +705,13 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   const uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
   uint16_t* orow = static_cast<uint16_t*>(a.out) + row * a.out_stride;
+  if (tid == 0 && v_end > v_begin && blockIdx.x < a.prefetch_ctas) {  // pass 1's first chunk
+    const uint64_t bytes = static_cast<uint64_t>(min(U * nthreads, v_end - v_begin)) * VEC;
+    prefetch_l2(xr + static_cast<int64_t>(v_begin) * EPV, bytes);
+    if constexpr (RES) prefetch_l2(rr + static_cast<int64_t>(v_begin) * EPV, bytes);
+  }
+  pdl_wait();
+  if constexpr (CLUSTER) cluster_arrive_relaxed();  // phase 1: completes once every peer is running
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
 
@@ -729,6 +752,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
     total = warp_sum(lane < static_cast<int>(csize) ? cta_part[lane] : 0.f);
   }
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
+  if (a.early_trigger) pdl_trigger();
 
   // Pass 2 reads the values this thread wrote (residual) or read (input) in pass 1.
   const uint16_t* src = RES ? rr : xr;
@@ -750,7 +774,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
       }
     }
   }
-  pdl_trigger();
+  if (!a.early_trigger) pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------

@@ -72,6 +72,47 @@ int current_device(const DeviceInfo** out) {
   return HPRN_OK;
 }
 
+int resident_ctas_per_sm(const DeviceInfo* dev, const void* fn, int threads, size_t smem) {
+  struct Entry {
+    int device;
+    const void* fn;
+    int threads;
+    size_t smem;
+    int ctas;
+  };
+  // A small per-thread cache in front of the shared table keeps the lock off
+  // the launch path after a thread's first call with each kernel shape.
+  constexpr int kLocal = 16;
+  thread_local Entry local[kLocal] = {};
+  const size_t slot = (reinterpret_cast<uintptr_t>(fn) / 16 + static_cast<size_t>(threads) +
+                       static_cast<size_t>(dev->device) * 7) % kLocal;
+  Entry& l = local[slot];
+  if (l.fn == fn && l.device == dev->device && l.threads == threads && l.smem == smem)
+    return l.ctas;
+  static std::mutex mu;
+  static Entry table[1024];
+  static int used = 0;
+  int ctas = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (table[i].fn == fn && table[i].device == dev->device && table[i].threads == threads &&
+          table[i].smem == smem) {
+        ctas = table[i].ctas;
+        break;
+      }
+    if (ctas < 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, fn, threads, smem) != cudaSuccess) {
+        cudaGetLastError();  // the query's error is not the caller's
+        return 0;
+      }
+      if (used < 1024) table[used++] = Entry{dev->device, fn, threads, smem, ctas};
+    }
+  }
+  l = Entry{dev->device, fn, threads, smem, ctas};
+  return ctas;
+}
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -402,17 +402,39 @@ __device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 
 }
 
 // ---------------------------------------------------------------------------
-// Programmatic dependent launch.  pdl_wait() at kernel entry, before the
-// first global-memory access: blocks until the grid this one depends on (if it
-// was launched that way) has completed and its memory is visible.
-// pdl_trigger() after the kernel's last store: a following kernel launched
-// with programmatic stream serialization may then be scheduled once every CTA
-// of this grid has reached it (or exited), so its launch overlaps this grid's
-// drain.  Triggering at entry instead let the next grid's CTAs take SM slots
-// and wait while this grid was still running: single-wave launches (decode
-// batches) then took up to 40% longer than with no programmatic launch at all.
-// With no programmatic dependency both are no-ops.
+// Programmatic dependent launch.  pdl_wait() before the kernel's first
+// global-memory load or store (only L2 prefetches come before it): blocks
+// until the grid this one depends on (if it was launched that way) has
+// completed and its memory is visible.  pdl_trigger() once a CTA's row
+// reductions are done (or after its last store; a launch knob): a following
+// kernel launched with programmatic stream serialization may then be scheduled
+// once every CTA of this grid has reached it (or exited), so its launch and its
+// L2 prefetch overlap this grid's epilogue and drain; it still reads nothing
+// before this grid has completed.  Triggering at kernel entry instead let the
+// next grid's CTAs take SM slots and wait while this grid was still running:
+// single-wave launches (decode batches) then took up to 40% longer than with no
+// programmatic launch at all.  With no programmatic dependency both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Asks L2 to fetch [p, p + bytes) from DRAM: one bulk prefetch, which the
+// TMA unit turns into line reads, so one thread covers a whole row slice at
+// no register cost to the others.  Kernels issue it before pdl_wait() for the
+// data they load first, so those DRAM reads overlap the preceding grid's
+// drain and the dependency wait instead of following them.  It is a hint: it
+// changes no register, shared-memory or memory contents, and the loads after
+// the wait return the preceding grid's writes whether or not the lines were
+// fetched before them (a prefetch is not a memory operation of the PTX memory
+// consistency model).  The range is widened to whole 16-byte granules, as the
+// instruction requires; a granule never straddles a page, so the widened
+// range is mapped wherever [p, p + bytes) is.  bytes > 0.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint64_t bytes) {
+  const uint64_t a = reinterpret_cast<uint64_t>(p);
+  const uint64_t lo = a & ~uint64_t{15};
+  const uint32_t n = static_cast<uint32_t>(((a + bytes + 15) & ~uint64_t{15}) - lo);
+  asm volatile(
+      "{\n\t.reg .u64 g;\n\tcvta.to.global.u64 g, %0;\n\t"
+      "cp.async.bulk.prefetch.L2.global [g], %1;\n\t}" ::"l"(lo), "r"(n));
+}
 
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -3,7 +3,7 @@
     python -m hp_rms_norm_b200.tune [--rows 4096] [--hidden 1024,2048,...]
                                     [--dtype bf16|fp16] [--warm] [--json out.json]
                                     [--no-tma | --tma-only] [--isolated] [--copy]
-                                    [--default-only]
+                                    [--default-only] [--knobs]
                                     [--variant fused|fused_out|plain|fused_fp8s|fused_fp8d|
                                                plain_fp8s|plain_fp8d|fused_nvfp4|plain_nvfp4|
                                                fused_fp8g|plain_fp8g]
@@ -14,7 +14,12 @@ heuristic's choice.  Candidates: warp rows (one warp per row, or several
 short rows per warp), one CTA per row and clusters of 2/4/8 CTAs at 32-byte
 vectors, one CTA per row at 16-byte vectors, two passes (one CTA or a
 cluster per row) past 4096 vectors, and TMA-staged rows (unless
-``--no-tma``).  ``--copy`` also times torch's ``copy_`` of the same bytes.  Timing: a CUDA graph of back-to-back launches over
+``--no-tma``).  ``--copy`` also times torch's ``copy_`` of the same bytes.  ``--knobs``
+times the default plan under each pair of launch knobs instead
+(``default:pf<p>:et<e>``: L2 prefetch before the programmatic-launch wait in
+no CTA, the first wave or every CTA; dependents triggered after the last store
+or after the row reduction), one process per pair, which is how
+``default_knobs`` in csrc/rms_norm.cu was fitted.  Timing: a CUDA graph of back-to-back launches over
 rotating buffer sets of at least 600 MB, so every launch reads cold data (or
 one buffer set with ``--warm``), replayed three times after one warm replay;
 with ``--isolated``, the median of single launches each preceded by an L2
@@ -209,19 +214,23 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
                               code, form, scale.data_ptr(), row_scales.data_ptr(), s)
 
         timings = {}
+        touched = False
         try:
             plans = candidates(h // 16, variant == "fused") if h % 16 == 0 and not default_only \
                 else []
             if form == capi.OUT_SAME and (tma or tma_only) and h % 8 == 0 and not default_only:
                 plans = (plans if not tma_only else []) + tma_candidates(h, res_needed)
+
             for p in plans:
+                touched = True
                 capi.set_plan_override(p)
                 try:
                     timings[p] = round(time_us(run, nsets), 2)
                 except capi.HprnError:
                     pass  # plan not compiled for this variant (e.g. over its launch bound)
         finally:
-            capi.set_plan_override(None)
+            if touched:  # an override from HP_RMS_NORM_PLAN stays in force otherwise
+                capi.set_plan_override(None)
         default = capi.plan(rows, h, code, xs[0].data_ptr(), rs[0].data_ptr()) \
             if variant == "fused" else "default"
         t_default = round(time_us(run, nsets), 2)
@@ -247,6 +256,46 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
     return results
 
 
+KNOBS = [f"default:pf{pf}:et{et}" for pf in (0, 1, 2) for et in (0, 1)]
+
+
+def knob_sweep(a, reps: int = 3) -> None:
+    """Times the default plan under every pair of launch knobs, each pair in
+    its own process (HP_RMS_NORM_PLAN=default:pf<p>:et<e>), the pairs taken in
+    turn `reps` times; prints the median per shape.  One process per pair
+    because timings drift within a long-running process by more than the
+    knobs' effect on short launches."""
+    import os
+    import subprocess
+    import sys
+    import tempfile
+
+    runs = {k: [] for k in KNOBS}
+    args = ["--rows", str(a.rows), "--hidden", a.hidden, "--dtype", a.dtype,
+            "--variant", a.variant, "--default-only", "--no-tma"]
+    if a.warm:
+        args.append("--warm")
+    with tempfile.TemporaryDirectory() as tmp:
+        for rep in range(reps):
+            for k in KNOBS:
+                out = os.path.join(tmp, "r.json")
+                env = dict(os.environ, HP_RMS_NORM_PLAN=k)
+                subprocess.run([sys.executable, "-m", "hp_rms_norm_b200.tune", *args, "--json", out],
+                               env=env, check=True, stdout=subprocess.DEVNULL)
+                with open(out) as f:
+                    runs[k].append(json.load(f))
+    print(f"{a.variant} rows={a.rows} {'warm' if a.warm else 'cold'}: median us of {reps} processes")
+    print(f"{'hidden':>7} " + " ".join(f"{k[8:]:>10}" for k in KNOBS))
+    table = {}
+    for h in a.hidden.split(","):
+        meds = [sorted(r[h]["default_us"] for r in runs[k])[reps // 2] for k in KNOBS]
+        table[h] = dict(zip(KNOBS, meds))
+        print(f"{h:>7} " + " ".join(f"{m:>10.2f}" for m in meds))
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump(table, f, indent=1)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--rows", type=int, default=4096)
@@ -263,7 +312,12 @@ def main() -> None:
                     help="also time torch's copy_ of the same bytes, the same way")
     ap.add_argument("--default-only", action="store_true",
                     help="time only the built-in heuristic's plan (e.g. under an ncu capture)")
+    ap.add_argument("--knobs", action="store_true",
+                    help="time the default plan under every pair of launch knobs")
     a = ap.parse_args()
+    if a.knobs:
+        knob_sweep(a)
+        return
     res = sweep(a.rows, [int(h) for h in a.hidden.split(",")], a.dtype, a.warm, a.variant,
                 tma=not a.no_tma, tma_only=a.tma_only, isolated=a.isolated, copy=a.copy,
                 default_only=a.default_only)

@@ -236,7 +236,14 @@ HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const v
 /*
  * Tuning hook: force the launch plan of every later hprn_rms_norm* call in
  * this process (same string format as hprn_rms_norm_plan; NULL or "" restores
- * the built-in heuristic).  The HP_RMS_NORM_PLAN environment variable, read at
+ * the built-in heuristic).  A plan may end in ":pf<F>:et<E>", two launch knobs
+ * that change timing only, never results: F is the L2 prefetch each CTA issues
+ * for its first rows before waiting on the preceding grid (0 none, 1 the
+ * grid's first wave of CTAs, 2 every CTA) and E where dependents are triggered
+ * (0 after the last store, 1 after the row reduction); without them the plan's
+ * defaults apply.  "default:pf<F>:et<E>" keeps the built-in plan and sets only
+ * the knobs.  hprn_rms_norm_plan echoes knobs an override names.  The
+ * HP_RMS_NORM_PLAN environment variable, read at
  * the first call, sets the same override.  A forced plan that does not fit a
  * call makes that call fail with HPRN_ERR_INVALID_ARGUMENT.  Process-global
  * (safe to call concurrently with launches): meant for benchmarks and

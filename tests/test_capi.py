@@ -194,6 +194,35 @@ def test_plan_override_parsing():
     assert capi.plan(4096, 4096).startswith("cta:")
 
 
+@pytest.mark.parametrize("bad", [
+    "default:pf3:et0", "default:pf1:et2", "default:pf1", "default:pf1:et1x",
+    "cta:vec32:vpt1:tpr256:cluster1:rpc1:pf1", "cta:vec32:vpt1:tpr256:cluster1:rpc1:pf-1:et0",
+    "cta:vec32:vpt1:tpr256:cluster1:rpc1 ", "cta:vec32:vpt1:tpr256:cluster1:rpc1:et1:pf1",
+])
+def test_plan_override_rejects_malformed_knobs(bad):
+    expect_error(lambda: capi.set_plan_override(bad), capi.ERR_INVALID_ARGUMENT, "unparsable")
+    capi.set_plan_override(None)
+
+
+def test_plan_override_knobs_are_echoed():
+    """Launch knobs (L2 prefetch scope, trigger point) are implied by the plan
+    unless an override names them: "default:pf<p>:et<e>" keeps the default plan
+    and sets only the knobs; a full plan may carry them as a suffix."""
+    base = capi.plan(4096, 4096)
+    assert ":pf" not in base
+    try:
+        capi.set_plan_override("default:pf0:et1")
+        assert capi.plan(4096, 4096) == base + ":pf0:et1"
+        assert capi.plan(4096, 1024) == capi.plan(4096, 1024).split(":pf")[0] + ":pf0:et1"
+        capi.set_plan_override("cta:vec32:vpt2:tpr128:cluster1:rpc1:pf1:et0")
+        assert capi.plan(4096, 4096) == "cta:vec32:vpt2:tpr128:cluster1:rpc1:pf1:et0"
+        capi.set_plan_override("cta:vec32:vpt2:tpr128:cluster1:rpc1")
+        assert capi.plan(4096, 4096) == "cta:vec32:vpt2:tpr128:cluster1:rpc1"
+    finally:
+        capi.set_plan_override(None)
+    assert capi.plan(4096, 4096) == base
+
+
 def test_wait_timeouts_needs_a_count_pointer():
     lib = capi.load()
     assert lib.hprn_wait_timeouts(None, 0) == capi.ERR_INVALID_ARGUMENT

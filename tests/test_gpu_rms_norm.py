@@ -387,6 +387,40 @@ def test_pdl_chains_match_plain_launches(cuda, hidden):
             assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
+KNOBS = [f"default:pf{pf}:et{et}" for pf in (0, 1, 2) for et in (0, 1)]
+
+
+@pytest.mark.parametrize("knobs", KNOBS)
+@pytest.mark.parametrize("rows,hidden", [(512, 1024), (600, 4096), (300, 24576), (64, 65536),
+                                         (4, 1 << 18)])
+def test_launch_knobs_keep_results(cuda, knobs, rows, hidden):
+    """The launch knobs only move work in time: an L2 prefetch issued before
+    the programmatic-launch wait (on lines the preceding call is still
+    writing), and the point where dependents are triggered.  Dependent chains
+    under every pair give the bits of plain launches (warp, CTA, cluster and
+    two-pass kernels; grids of more than one wave)."""
+    x0, w, r0, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=hidden + 11, device=cuda)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def chain(flags):
+        x, r, out = x0.clone(), r0.clone(), torch.empty_like(x0)
+        for _ in range(3):
+            capi.rms_norm_tensors(x, w, r, eps, stream=stream, flags=flags)
+        capi.relu_tensors(out, x, stream=stream, flags=flags)
+        torch.cuda.synchronize()
+        return x, r, out
+
+    want = chain(0)
+    capi.set_plan_override(knobs)
+    try:
+        assert capi.plan(rows, hidden).endswith(knobs[7:])
+        got = chain(capi.LAUNCH_PDL)
+    finally:
+        capi.set_plan_override(None)
+    for a, b in zip(want, got):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
 def test_launch_flags_validated(cuda):
     x, w, r, eps = make_inputs(4, 256, torch.bfloat16, "c0", seed=1, device=cuda)
     with pytest.raises(capi.HprnError, match="unknown launch flags"):

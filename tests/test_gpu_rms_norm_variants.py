@@ -114,6 +114,26 @@ def test_variant_every_plan_kind(cuda, variant, rows, hidden, plan):
         capi.set_plan_override(None)
 
 
+@pytest.mark.parametrize("knobs", [f"default:pf{pf}:et{et}" for pf in (0, 1, 2) for et in (0, 1)])
+@pytest.mark.parametrize("rows,hidden", [(600, 4096), (300, 32768)])
+@pytest.mark.parametrize("variant", VARIANTS)
+def test_variant_launch_knobs_keep_results(cuda, variant, rows, hidden, knobs):
+    """Every pair of launch knobs (L2 prefetch scope, trigger point) gives the
+    default launch's bits for every form, on grids of more than one wave."""
+    x, w, r, eps = make_inputs(rows, hidden, torch.bfloat16, "c0", seed=hidden + 3, device=cuda)
+    r1, r2 = r.clone(), r.clone()
+    want = run_variant(variant, x, w, r1, eps, cuda)
+    capi.set_plan_override(knobs)
+    try:
+        got = run_variant(variant, x, w, r2, eps, cuda)
+    finally:
+        capi.set_plan_override(None)
+    assert torch.equal(r1.view(torch.int16), r2.view(torch.int16))
+    for a, b in zip(want, got):
+        if a is not None:
+            assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_edge_operands_vs_oracle(cuda, variant, dtype):
