@@ -291,10 +291,14 @@ Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
 //   * past that, and from 64 KB for the fused 16-bit form, it pays in the
 //     first wave only (4096 x 32768 fused: 157.6 us, 159.3 with every CTA,
 //     157.8 with none; 4096 x 16384: 79.9 against 80.4 with every CTA), and
-//     so it does for the plain NVFP4 and dynamic or per-group fp8 forms at
-//     four vectors per thread (plain NVFP4 at 4096 x 32768: 60.4 vs 63.5).
+//     so it does for the plain dynamic fp8 form at four vectors per thread
+//     (4096 x 32768: 65.4 vs 66.4).
 void default_knobs(Plan* p, const Variant& var) {
-  if (p->kind == kTma) {  // the TMA-staged kernel stages rows itself and triggers at its end
+  // The TMA-staged kernel stages rows itself and triggers at its end; CTA
+  // kernels of the issue-bound plain quantised forms are built without the
+  // knobs (cta_has_knobs).
+  if (p->kind == kTma || ((p->kind == kCtaRows || p->kind == kClusterRows) &&
+                          !cta_has_knobs(var.res, var.out, p->vpt))) {
     p->prefetch = kPrefetchNone;
     p->early = 0;
     return;
@@ -304,8 +308,7 @@ void default_knobs(Plan* p, const Variant& var) {
     const int threads = p->kind == kWarpRows ? p->rows_per_cta * p->tpr : p->tpr;
     const int vpt = p->kind == kTwoPass ? kTwoPassUnroll : p->vpt;  // two passes: its first chunk
     const int64_t bytes = static_cast<int64_t>(threads) * vpt * p->vec * (var.res ? 2 : 1);
-    const bool issue_bound_plain =
-        !var.res && var.out != kOutSame && var.out != kOutFp8Static && p->vpt >= 4;
+    const bool issue_bound_plain = !var.res && var.out == kOutFp8Dynamic && p->vpt >= 4;
     const bool big = bytes > 65536 || (bytes == 65536 && var.full());
     p->prefetch = (big || issue_bound_plain) ? kPrefetchFirstWave : kPrefetchAll;
   }

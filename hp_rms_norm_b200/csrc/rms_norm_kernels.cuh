@@ -488,9 +488,9 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
       }
     }
   }
+  float inv_scale = static_inv_scale<OUT>(a);
   const float inv = rsqrtf(fmaf(lane_group_sum(a0 + a1, lpr), a.inv_hidden, a.eps));
   if (a.early_trigger) pdl_trigger();
-  float inv_scale = static_inv_scale<OUT>(a);
   if constexpr (OUT == kOutFp8Dynamic) {
     const float scale = fmaxf(lane_group_max(m, lpr) * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
@@ -534,9 +534,20 @@ __host__ __device__ constexpr int cta_min_blocks(int vpt, bool cluster, bool res
 // pushed into every peer's shared memory, so each CTA finishes each reduction
 // locally after one cluster barrier and no CTA touches a peer's memory
 // afterwards.
+// Whether a CTA kernel instance has the launch knobs (L2 prefetch before the
+// dependency wait, trigger after the reduction).  The plain NVFP4 and
+// per-group fp8 forms at four vectors per thread are issue-bound, and with
+// the knobs' code compiled in they ran 1.5-2% slower at hidden 16384-32768
+// even with both knobs off (plain NVFP4 at 4096 x 32768: 60.6 against 59.5
+// us); they keep their trigger at the end and no prefetch.
+__host__ __device__ constexpr bool cta_has_knobs(bool res, int out, int vpt) {
+  return res || (out != kOutNvfp4 && out != kOutFp8Group) || vpt < 4;
+}
+
 template <typename T, int VEC, int VPT, bool CLUSTER, bool RES, int OUT>
 __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUSTER, RES, OUT))
     rms_norm_cta_rows(RmsArgs a) {
+  constexpr bool kKnobs = cta_has_knobs(RES, OUT, VPT);
   constexpr int EPV = Vec<VEC>::kElems;
   __shared__ float warp_part[32];
   __shared__ float warp_amax[32];
@@ -562,7 +573,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
   }
   const uint16_t* xr = a.x + row * a.x_stride;
   uint16_t* rr = RES ? a.r + row * a.r_stride : nullptr;
-  if (tid == 0 && v_end > v_begin && blockIdx.x < a.prefetch_ctas) {
+  if (kKnobs && tid == 0 && v_end > v_begin && blockIdx.x < a.prefetch_ctas) {
     const uint64_t bytes = static_cast<uint64_t>(v_end - v_begin) * VEC;
     prefetch_l2(xr + static_cast<int64_t>(v_begin) * EPV, bytes);
     if constexpr (RES) prefetch_l2(rr + static_cast<int64_t>(v_begin) * EPV, bytes);
@@ -620,6 +631,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
       }
     }
   }
+  float inv_scale = static_inv_scale<OUT>(a);  // read before the barrier hides its latency
   const float wsum = warp_sum(a0 + a1);
   if constexpr (kAmax) m = warp_max(m);
   if (lane == 0) {
@@ -641,8 +653,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
     if constexpr (kAmax) amax = warp_max(lane < static_cast<int>(csize) ? cta_amax[lane] : 0.f);
   }
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
-  if (a.early_trigger) pdl_trigger();
-  float inv_scale = static_inv_scale<OUT>(a);
+  if (kKnobs && a.early_trigger) pdl_trigger();
   if constexpr (kAmax) {
     const float scale = fmaxf(amax * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
@@ -660,7 +671,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
                              inv_scale);
     }
   }
-  if (!a.early_trigger) pdl_trigger();
+  if (!kKnobs || !a.early_trigger) pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------

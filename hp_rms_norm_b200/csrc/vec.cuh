@@ -436,8 +436,11 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint64_t bytes) {
       "cp.async.bulk.prefetch.L2.global [g], %1;\n\t}" ::"l"(lo), "r"(n));
 }
 
+// No memory clobber: the trigger orders nothing (a dependent still waits for
+// this grid's completion before it reads), so loads and stores stay free to
+// move across it.
 __device__ __forceinline__ void pdl_trigger() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
 }
 
 }  // namespace hprn
