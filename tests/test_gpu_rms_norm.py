@@ -298,6 +298,21 @@ def test_deterministic_and_graph_capturable(cuda):
     assert torch.equal(r1.view(torch.int16), r2.view(torch.int16))
 
 
+def test_first_calls_inside_graph_capture(cuda):
+    """A process whose first calls of each kernel shape happen inside a CUDA
+    graph capture (the library queries a kernel's occupancy once per device
+    on its first launch, to size the L2 prefetch) captures, replays and gives
+    the bits of eager launches (tests/graph_first_call_worker.py, run in a
+    fresh process so no kernel shape has been launched before)."""
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    p = subprocess.run([sys.executable, os.path.join(root, "tests", "graph_first_call_worker.py")],
+                       cwd=root, capture_output=True, text=True, timeout=300)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-3000:]
+
+
 REF_SO = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref",
                       "libhp_rms_norm_ref.so")
 
