@@ -30,13 +30,14 @@ struct Plan {
   int rows_per_cta = 1;  // warp kind: rows per CTA; tma kind: ring depth (rows in flight per CTA)
   // Launch knobs (-1: the default for the plan, see default_knobs):
   int prefetch = -1;  // L2 prefetch before the programmatic-launch wait: 0 none,
-                      // 1 the grid's first wave of CTAs, 2 every CTA
+                      // 1 the grid's first wave of CTAs, 2 every CTA, 3 the first
+                      // wave, and every CTA also the row one wave ahead
   int early = -1;     // 1: trigger dependents after the row reduction, 0: after the last store
   bool knobs_given = false;  // set by parse_plan when the string carried both knobs
   bool knobs_only = false;   // override "default:pf<p>:et<e>": the default plan, these knobs
 };
 
-enum Prefetch { kPrefetchNone = 0, kPrefetchFirstWave = 1, kPrefetchAll = 2 };
+enum Prefetch { kPrefetchNone = 0, kPrefetchFirstWave = 1, kPrefetchAll = 2, kPrefetchAhead = 3 };
 
 // Kernel family of one call: residual or not, and the output form.
 struct Variant {
@@ -277,22 +278,25 @@ Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
 }
 
 // Fills the launch knobs a plan leaves at -1 (default_plan's plans, and
-// overrides without ":pf..:et.."), from cold-L2 timings of every combination
+// overrides without ":pf..:et.."), from cold-L2 timings of the combinations
 // (tune.py --knobs: one process per combination, three runs each) at batch
-// 4096 x hidden 1024-32768 for the 16-bit, NVFP4, dynamic and per-group fp8
-// forms, and at 64 rows x hidden 4096-1M (cluster and two-pass kernels):
+// 4096 x hidden 1024-32768 for every output form, and at 64 rows x hidden
+// 4096-1M (cluster and two-pass kernels):
 //   * triggering dependents after the row reduction is as fast or faster
 //     everywhere (4096 x 1024: fused 6.07 vs 6.12 us, plain NVFP4 3.75 vs
 //     4.14, fused per-group fp8 6.29 vs 6.80; 64 x 262144: 24.8 vs 25.4);
-//   * the L2 prefetch pays in every CTA while one CTA prefetches less than
-//     64 KB (fused 4096 x 1024 / 4096: 6.07 / 21.1 us, against 6.38 / 21.5
-//     without it; at 4096 x 4096 about half of the gain comes from the first
-//     wave alone);
-//   * past that, and from 64 KB for the fused 16-bit form, it pays in the
-//     first wave only (4096 x 32768 fused: 157.6 us, 159.3 with every CTA,
-//     157.8 with none; 4096 x 16384: 79.9 against 80.4 with every CTA), and
-//     so it does for the plain dynamic fp8 form at four vectors per thread
-//     (4096 x 32768: 65.4 vs 66.4).
+//   * the L2 prefetch of the first wave's rows, with every CTA also
+//     prefetching the row of the CTA one wave after it, is the fastest mode
+//     for the fused forms and plain 16-bit rows of every length (fused 4096 x
+//     4096 / 16384 / 32768: 20.78 / 79.15 / 156.4 us, against 21.15 / 80.2 /
+//     158.6 with every CTA prefetching only its own row; plain 4096 x 4096:
+//     10.66 vs 11.62), and for the plain quantised forms from 1024 vectors
+//     per CTA (512 for per-row fp8);
+//   * shorter plain quantised rows (their CTAs issue-bound and short-lived)
+//     and the two-pass kernel do better prefetching only their own rows: in
+//     every CTA while one CTA prefetches less than 64 KB (plain static fp8 at
+//     4096 x 4096: 9.74 vs 10.20 with the row ahead), in the first wave past
+//     that (and from 64 KB for the fused form).
 void default_knobs(Plan* p, const Variant& var) {
   // The TMA-staged kernel stages rows itself and triggers at its end; CTA
   // kernels of the issue-bound plain quantised forms are built without the
@@ -305,12 +309,19 @@ void default_knobs(Plan* p, const Variant& var) {
   }
   if (p->early < 0) p->early = 1;
   if (p->prefetch < 0) {
+    // Vectors of one row a CTA holds, and the bytes its own prefetch covers.
+    const int slice = p->tpr * p->vpt;
     const int threads = p->kind == kWarpRows ? p->rows_per_cta * p->tpr : p->tpr;
     const int vpt = p->kind == kTwoPass ? kTwoPassUnroll : p->vpt;  // two passes: its first chunk
     const int64_t bytes = static_cast<int64_t>(threads) * vpt * p->vec * (var.res ? 2 : 1);
-    const bool issue_bound_plain = !var.res && var.out == kOutFp8Dynamic && p->vpt >= 4;
-    const bool big = bytes > 65536 || (bytes == 65536 && var.full());
-    p->prefetch = (big || issue_bound_plain) ? kPrefetchFirstWave : kPrefetchAll;
+    const bool plain_quant = !var.res && var.out != kOutSame;
+    if (p->kind != kTwoPass &&
+        (!plain_quant || slice >= (var.out == kOutFp8Dynamic ? 512 : 1024))) {
+      p->prefetch = kPrefetchAhead;
+    } else {
+      const bool big = bytes > 65536 || (bytes == 65536 && var.full());
+      p->prefetch = big ? kPrefetchFirstWave : kPrefetchAll;
+    }
   }
 }
 
@@ -353,7 +364,7 @@ bool parse_plan(const std::string& s, Plan* p) {
   if (s.rfind("default:", 0) == 0) {
     int pf = -1, et = -1, end = 0;
     if (sscanf(s.c_str(), "default:pf%d:et%d%n", &pf, &et, &end) != 2 ||
-        static_cast<size_t>(end) != s.size() || pf < 0 || pf > 2 || et < 0 || et > 1)
+        static_cast<size_t>(end) != s.size() || pf < 0 || pf > 3 || et < 0 || et > 1)
       return false;
     p->prefetch = pf;
     p->early = et;
@@ -364,9 +375,9 @@ bool parse_plan(const std::string& s, Plan* p) {
   int vec, vpt, tpr, cluster, rpc, pf = -1, et = -1, end = 0;
   const int got = sscanf(s.c_str(), "%15[a-z]:vec%d:vpt%d:tpr%d:cluster%d:rpc%d%n:pf%d:et%d%n",
                          kind, &vec, &vpt, &tpr, &cluster, &rpc, &end, &pf, &et, &end);
-  // Six fields, optionally followed by both knobs (":pf<0|1|2>:et<0|1>"), and nothing else.
+  // Six fields, optionally followed by both knobs (":pf<0..3>:et<0|1>"), and nothing else.
   if ((got != 6 && got != 8) || static_cast<size_t>(end) != s.size()) return false;
-  if (got == 8 && (pf < 0 || pf > 2 || et < 0 || et > 1)) return false;
+  if (got == 8 && (pf < 0 || pf > 3 || et < 0 || et > 1)) return false;
   p->prefetch = got == 8 ? pf : -1;
   p->early = got == 8 ? et : -1;
   p->knobs_given = got == 8;
@@ -766,6 +777,7 @@ int make_plan(const Problem& q, const Variant& var, Plan* plan, RmsArgs* args) {
   a.stall_row = g_stall_row.load(std::memory_order_relaxed);
   a.wait_limit_ns = g_stall_wait_ns.load(std::memory_order_relaxed);
   a.prefetch_ctas = 0;  // set per launch
+  a.prefetch_ahead_rows = 0;
   a.early_trigger = p.early;
   *plan = p;
   *args = a;
@@ -843,10 +855,14 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
   const int64_t ctas_per_unit = clustered ? p.cluster : 1;
   const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
   const int threads = p.kind == kWarpRows ? p.rows_per_cta * p.tpr : p.tpr;
-  a.prefetch_ctas = p.prefetch == kPrefetchNone ? 0
-                    : p.prefetch == kPrefetchAll
-                        ? INT64_MAX
-                        : first_wave_ctas(dev, reinterpret_cast<const void*>(fn), threads);
+  const int64_t wave = p.prefetch == kPrefetchFirstWave || p.prefetch == kPrefetchAhead
+                           ? first_wave_ctas(dev, reinterpret_cast<const void*>(fn), threads)
+                           : 0;
+  a.prefetch_ctas = p.prefetch == kPrefetchAll ? INT64_MAX : wave;
+  // The row the CTA one wave later handles: a wave of CTAs covers wave /
+  // ctas_per_unit row units of rows_per_unit rows.
+  a.prefetch_ahead_rows =
+      p.prefetch == kPrefetchAhead ? wave / ctas_per_unit * rows_per_unit : 0;
 
   int64_t done = 0;
   while (done < a.rows) {

@@ -106,10 +106,31 @@ struct RmsArgs {
   // CTAs blockIdx.x < prefetch_ctas prefetch their first rows into L2 before
   // the programmatic-launch wait (0: none; the grid's first wave; or all).
   int64_t prefetch_ctas;
+  // > 0: after issuing its own loads, each CTA also prefetches its slice of
+  // the row this many rows ahead, the row of the CTA that will take its place
+  // one wave later.
+  int64_t prefetch_ahead_rows;
   // Nonzero: trigger dependents (pdl_trigger) right after the row reduction
   // instead of after the last store.
   int32_t early_trigger;
 };
+
+// Prefetches into L2 the vectors [v_begin, v_end) of the row
+// a.prefetch_ahead_rows after `row` (input, and residual with RES), when that
+// row is part of this launch.  One thread per row slice calls it, after its
+// CTA's own loads are issued: the DRAM reads of the row a CTA of the next wave
+// will load then overlap this CTA's reduction and epilogue, without registers.
+template <int VEC, bool RES>
+__device__ __forceinline__ void prefetch_row_ahead(const RmsArgs& a, int64_t row, int v_begin,
+                                                   int v_end) {
+  const int64_t ahead = row + a.prefetch_ahead_rows;
+  if (a.prefetch_ahead_rows > 0 && ahead < a.rows && v_end > v_begin) {
+    const int64_t first = static_cast<int64_t>(v_begin) * Vec<VEC>::kElems;
+    const uint64_t bytes = static_cast<uint64_t>(v_end - v_begin) * VEC;
+    prefetch_l2(a.x + ahead * a.x_stride + first, bytes);
+    if constexpr (RES) prefetch_l2(a.r + ahead * a.r_stride + first, bytes);
+  }
+}
 
 // Element pairs go through Blackwell's packed fp32 instructions
 // (__fadd2_rn / __fmul2_rn / __ffma2_rn: add/mul/fma.rn.f32x2), and squares
@@ -455,6 +476,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
       if constexpr (RES) rv[j] = ld_stream<VEC>(rr + v * EPV, pol_stream);
     }
   }
+  if (active && sub == 0) prefetch_row_ahead<VEC, RES>(a, row, 0, a.nvec);
   float a0 = 0.f, a1 = 0.f;
   // Dynamic fp8: max |r * w| does not depend on inv, so it is reduced next to
   // the sum of squares and scaled by inv once (see prod_amax).  The products
@@ -598,6 +620,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
       if constexpr (RES) rv[j] = ld_stream<VEC>(rr + static_cast<int64_t>(v) * EPV, pol_stream);
     }
   }
+  if (kKnobs && tid == 0) prefetch_row_ahead<VEC, RES>(a, row, v_begin, v_end);
   // Dynamic fp8: max |r * w| does not depend on inv, so it travels with the
   // sum of squares through the same barrier (and cluster phase) and is scaled
   // by inv once at the end (see prod_amax).  The products r * w are held
@@ -727,6 +750,7 @@ __global__ void __launch_bounds__(kTwoPassThreads) rms_norm_two_pass(RmsArgs a) 
   }
   pdl_wait();
   if constexpr (CLUSTER) cluster_arrive_relaxed();  // phase 1: completes once every peer is running
+  if (tid == 0) prefetch_row_ahead<VEC, RES>(a, row, v_begin, min(v_begin + U * nthreads, v_end));
   const uint64_t pol_stream = policy_evict_first();
   const uint64_t pol_keep = policy_evict_last();
 

@@ -239,7 +239,8 @@ HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const v
  * the built-in heuristic).  A plan may end in ":pf<F>:et<E>", two launch knobs
  * that change timing only, never results: F is the L2 prefetch each CTA issues
  * for its first rows before waiting on the preceding grid (0 none, 1 the
- * grid's first wave of CTAs, 2 every CTA) and E where dependents are triggered
+ * grid's first wave of CTAs, 2 every CTA, 3 the first wave, with every CTA also
+ * prefetching the row of the CTA one wave later) and E where dependents are triggered
  * (0 after the last store, 1 after the row reduction); without them the plan's
  * defaults apply.  "default:pf<F>:et<E>" keeps the built-in plan and sets only
  * the knobs.  hprn_rms_norm_plan echoes knobs an override names.  The
