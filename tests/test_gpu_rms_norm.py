@@ -298,6 +298,53 @@ def test_deterministic_and_graph_capturable(cuda):
     assert torch.equal(r1.view(torch.int16), r2.view(torch.int16))
 
 
+def test_concurrent_host_threads(cuda):
+    """Eight host threads call the C ABI at once, each on its own stream with
+    its own shape (kernels whose occupancy the per-device cache may not hold
+    yet are launched concurrently); every result equals the same call made
+    alone afterwards."""
+    import threading
+
+    shapes = [(257, 1024), (300, 2560), (129, 4096), (64, 7168), (96, 12288), (40, 20480),
+              (16, 40960), (8, 1 << 17)]
+    inputs = [make_inputs(rows, hidden, torch.bfloat16, "c0", seed=rows + hidden, device=cuda)
+              for rows, hidden in shapes]
+    torch.cuda.synchronize()
+    got = [None] * len(shapes)
+    errors = []
+
+    def work(k):
+        try:
+            x0, w, r0, eps = inputs[k]
+            s = torch.cuda.Stream(device=cuda)
+            with torch.cuda.stream(s):
+                x, r = x0.clone(), r0.clone()
+                for _ in range(3):  # same inputs each time: the last call's result is compared
+                    x.copy_(x0)
+                    r.copy_(r0)
+                    capi.rms_norm_tensors(x, w, r, eps, stream=s.cuda_stream)
+            s.synchronize()
+            got[k] = (x, r)
+        except Exception as e:  # reported below, on the main thread
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=work, args=(k,)) for k in range(len(shapes))]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    want = []
+    for x0, w, r0, eps in inputs:
+        x, r = x0.clone(), r0.clone()
+        capi.rms_norm_tensors(x, w, r, eps)
+        want.append((x, r))
+    torch.cuda.synchronize()
+    for (wx, wr), (gx, gr) in zip(want, got):
+        assert torch.equal(wx.view(torch.int16), gx.view(torch.int16))
+        assert torch.equal(wr.view(torch.int16), gr.view(torch.int16))
+
+
 def test_first_calls_inside_graph_capture(cuda):
     """A process whose first calls of each kernel shape happen inside a CUDA
     graph capture (the library queries a kernel's occupancy once per device
