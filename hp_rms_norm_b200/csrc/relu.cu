@@ -60,6 +60,7 @@ struct ReluArgs {
   int64_t out_stride;      // elements
   int64_t in_stride;
   int64_t prefetch_ctas;   // CTAs blockIdx.x < this (the first wave) prefetch into L2
+  int64_t prefetch_ahead;  // > 0: each CTA also prefetches the chunk of CTA blockIdx.x + this
   int64_t tail_begin;      // flat mode: first element not covered by vectors
   int64_t tail_end;
 };
@@ -84,6 +85,18 @@ __global__ void __launch_bounds__(256) relu_rows(ReluArgs a) {
   for (int k = 0; k < U; ++k) {
     const int64_t i = base + static_cast<int64_t>(k) * blockDim.x;
     if (i < a.nvec) v[k] = ld_stream<VEC>(src + i * EPV, pol);
+  }
+  // The chunk of the CTA one wave later (the one that takes this CTA's slot):
+  // its DRAM reads overlap this CTA's stores.  Config 3: 4096 x 14336 bf16 in
+  // 35.10 against 35.43 us, 8192 x 28672 fp16 in 136.71 against 137.10.  (The
+  // gated activations, issue-bound, were slower with it: GELU 63.4 vs 59.8.)
+  const int64_t later = static_cast<int64_t>(blockIdx.x) + a.prefetch_ahead;
+  if (threadIdx.x == 0 && a.prefetch_ahead > 0 && later < gridDim.x) {
+    const int64_t lrow = later / a.chunks_per_row;
+    const int64_t lfirst = (later - lrow * a.chunks_per_row) * (static_cast<int64_t>(blockDim.x) * U);
+    if (lfirst < a.nvec)
+      prefetch_l2(a.in + lrow * a.in_stride + lfirst * EPV,
+                  static_cast<uint64_t>(min(static_cast<int64_t>(blockDim.x) * U, a.nvec - lfirst)) * VEC);
   }
 #pragma unroll
   for (int k = 0; k < U; ++k) {
@@ -190,6 +203,7 @@ int hprn_relu_ex(void* out, const void* input, int64_t rows, int64_t hidden,
   if (grid > 2147483647LL) return fail(HPRN_ERR_INVALID_ARGUMENT, "tensor too large for one launch");
   ReluFn fn = dtype == HPRN_DTYPE_BF16 ? pick_relu<__nv_bfloat16>(vec) : pick_relu<__half>(vec);
   a.prefetch_ctas = first_wave_ctas(dev, reinterpret_cast<const void*>(fn), kReluThreads);
+  a.prefetch_ahead = a.prefetch_ctas;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
