@@ -32,9 +32,11 @@ struct Plan {
   int prefetch = -1;  // L2 prefetch before the programmatic-launch wait: 0 none,
                       // 1 the grid's first wave of CTAs, 2 every CTA, 3 the first
                       // wave, and every CTA also the row one wave ahead
-  int early = -1;     // 1: trigger dependents after the row reduction, 0: after the last store
+  int early = -1;     // where dependents are triggered: 0 after the last store, 1 after
+                      // the row reduction, 2 once the loads are issued (-1: by grid size)
   bool knobs_given = false;  // set by parse_plan when the string carried both knobs
   bool knobs_only = false;   // override "default:pf<p>:et<e>": the default plan, these knobs
+  bool trig_loads = false;   // launch: the kernel instance that triggers once its loads are issued
 };
 
 enum Prefetch { kPrefetchNone = 0, kPrefetchFirstWave = 1, kPrefetchAll = 2, kPrefetchAhead = 3 };
@@ -283,8 +285,13 @@ Plan default_plan(int nvec, int vec, bool residual, int out, int64_t rows) {
 // 4096 x hidden 1024-32768 for every output form, and at 64 rows x hidden
 // 4096-1M (cluster and two-pass kernels):
 //   * triggering dependents after the row reduction is as fast or faster
-//     everywhere (4096 x 1024: fused 6.07 vs 6.12 us, plain NVFP4 3.75 vs
-//     4.14, fused per-group fp8 6.29 vs 6.80; 64 x 262144: 24.8 vs 25.4);
+//     than after the last store everywhere (4096 x 1024: fused 6.07 vs 6.12
+//     us, plain NVFP4 3.75 vs 4.14, fused per-group fp8 6.29 vs 6.80; 64 x
+//     262144: 24.8 vs 25.4), and triggering once the loads are issued is
+//     faster still for grids of more than one wave (fused 4096 x 2048 / 4096
+//     / 8192: 10.40 / 19.82 / 39.16 us against 11.18 / 21.22 / 40.56) but
+//     slower for single-wave grids (128 x 4096 warm: 1.77 vs 1.61), so the
+//     trigger point is left to the launch (-1), which picks by grid size;
 //   * the L2 prefetch of the first wave's rows, with every CTA also
 //     prefetching the row of the CTA one wave after it, is the fastest mode
 //     for the fused forms and plain 16-bit rows of every length (fused 4096 x
@@ -307,7 +314,6 @@ void default_knobs(Plan* p, const Variant& var) {
     p->early = 0;
     return;
   }
-  if (p->early < 0) p->early = 1;
   if (p->prefetch < 0) {
     // Vectors of one row a CTA holds, and the bytes its own prefetch covers.
     const int slice = p->tpr * p->vpt;
@@ -364,7 +370,7 @@ bool parse_plan(const std::string& s, Plan* p) {
   if (s.rfind("default:", 0) == 0) {
     int pf = -1, et = -1, end = 0;
     if (sscanf(s.c_str(), "default:pf%d:et%d%n", &pf, &et, &end) != 2 ||
-        static_cast<size_t>(end) != s.size() || pf < 0 || pf > 3 || et < 0 || et > 1)
+        static_cast<size_t>(end) != s.size() || pf < 0 || pf > 3 || et < 0 || et > 2)
       return false;
     p->prefetch = pf;
     p->early = et;
@@ -375,9 +381,9 @@ bool parse_plan(const std::string& s, Plan* p) {
   int vec, vpt, tpr, cluster, rpc, pf = -1, et = -1, end = 0;
   const int got = sscanf(s.c_str(), "%15[a-z]:vec%d:vpt%d:tpr%d:cluster%d:rpc%d%n:pf%d:et%d%n",
                          kind, &vec, &vpt, &tpr, &cluster, &rpc, &end, &pf, &et, &end);
-  // Six fields, optionally followed by both knobs (":pf<0..3>:et<0|1>"), and nothing else.
+  // Six fields, optionally followed by both knobs (":pf<0..3>:et<0..2>"), and nothing else.
   if ((got != 6 && got != 8) || static_cast<size_t>(end) != s.size()) return false;
-  if (got == 8 && (pf < 0 || pf > 3 || et < 0 || et > 1)) return false;
+  if (got == 8 && (pf < 0 || pf > 3 || et < 0 || et > 2)) return false;
   p->prefetch = got == 8 ? pf : -1;
   p->early = got == 8 ? et : -1;
   p->knobs_given = got == 8;
@@ -462,36 +468,54 @@ bool plan_valid(const Plan& p, int nvec, int max_vec, const Variant& var, std::s
 
 using KernelFn = void (*)(RmsArgs);
 
+// The instance that triggers its dependents once its loads are issued (tl),
+// or the one whose trigger point is the runtime knob.
+template <typename T, int VEC, int VPT, bool RES, int OUT>
+KernelFn warp_fn(bool tl) {
+  return tl ? rms_norm_warp_rows<T, VEC, VPT, RES, OUT, true>
+            : rms_norm_warp_rows<T, VEC, VPT, RES, OUT, false>;
+}
+
+template <typename T, int VEC, int VPT, bool CL, bool RES, int OUT>
+KernelFn cta_fn(bool tl) {
+  if constexpr (!cta_has_knobs(RES, OUT, VPT)) {
+    return rms_norm_cta_rows<T, VEC, VPT, CL, RES, OUT, false>;
+  } else {
+    return tl ? rms_norm_cta_rows<T, VEC, VPT, CL, RES, OUT, true>
+              : rms_norm_cta_rows<T, VEC, VPT, CL, RES, OUT, false>;
+  }
+}
+
 template <typename T, int VEC, bool RES, int OUT>
-KernelFn pick_warp(int vpt) {
+KernelFn pick_warp(int vpt, bool tl) {
   if constexpr (RES && OUT == kOutSame) {
-    if (vpt == 3) return rms_norm_warp_rows<T, VEC, 3, RES, OUT>;
+    if (vpt == 3) return warp_fn<T, VEC, 3, RES, OUT>(tl);
   }
   switch (vpt) {
-    case 1: return rms_norm_warp_rows<T, VEC, 1, RES, OUT>;
-    case 2: return rms_norm_warp_rows<T, VEC, 2, RES, OUT>;
-    case 4: return rms_norm_warp_rows<T, VEC, 4, RES, OUT>;
+    case 1: return warp_fn<T, VEC, 1, RES, OUT>(tl);
+    case 2: return warp_fn<T, VEC, 2, RES, OUT>(tl);
+    case 4: return warp_fn<T, VEC, 4, RES, OUT>(tl);
   }
   return nullptr;
 }
 
 template <typename T, int VEC, bool CL, bool RES, int OUT>
-KernelFn pick_cta(int vpt) {
+KernelFn pick_cta(int vpt, bool tl) {
   if constexpr (RES && OUT == kOutSame) {
     if constexpr (VEC == 32) {
       switch (vpt) {
-        case 3: return rms_norm_cta_rows<T, VEC, 3, CL, RES, OUT>;
-        case 6: return rms_norm_cta_rows<T, VEC, 6, CL, RES, OUT>;
+        case 3: return cta_fn<T, VEC, 3, CL, RES, OUT>(tl);
+        case 6: return cta_fn<T, VEC, 6, CL, RES, OUT>(tl);
       }
     }
     if constexpr (!(CL && VEC == 4)) {
-      if (vpt == 8) return rms_norm_cta_rows<T, VEC, 8, CL, RES, OUT>;
+      if (vpt == 8) return cta_fn<T, VEC, 8, CL, RES, OUT>(tl);
     }
   }
   switch (vpt) {
-    case 1: return rms_norm_cta_rows<T, VEC, 1, CL, RES, OUT>;
-    case 2: return rms_norm_cta_rows<T, VEC, 2, CL, RES, OUT>;
-    case 4: return rms_norm_cta_rows<T, VEC, 4, CL, RES, OUT>;
+    case 1: return cta_fn<T, VEC, 1, CL, RES, OUT>(tl);
+    case 2: return cta_fn<T, VEC, 2, CL, RES, OUT>(tl);
+    case 4: return cta_fn<T, VEC, 4, CL, RES, OUT>(tl);
   }
   return nullptr;
 }
@@ -513,9 +537,9 @@ KernelFn pick_kind(const Plan& p) {
     case kTma:
       if constexpr ((VEC == 16 || VEC == 32) && OUT == kOutSame) return pick_tma<T, VEC, RES>(p.vpt);
       return nullptr;
-    case kWarpRows: return pick_warp<T, VEC, RES, OUT>(p.vpt);
-    case kCtaRows: return pick_cta<T, VEC, false, RES, OUT>(p.vpt);
-    case kClusterRows: return pick_cta<T, VEC, true, RES, OUT>(p.vpt);
+    case kWarpRows: return pick_warp<T, VEC, RES, OUT>(p.vpt, p.trig_loads);
+    case kCtaRows: return pick_cta<T, VEC, false, RES, OUT>(p.vpt, p.trig_loads);
+    case kClusterRows: return pick_cta<T, VEC, true, RES, OUT>(p.vpt, p.trig_loads);
     default:
       if constexpr (OUT == kOutSame)
         return p.cluster > 1 ? rms_norm_two_pass<T, VEC, RES, true> : rms_norm_two_pass<T, VEC, RES, false>;
@@ -849,15 +873,22 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
   KernelFn fn = pick_kernel(dtype, p, var);
   if (!fn) return fail(HPRN_ERR_INVALID_ARGUMENT, "no kernel for plan " + plan_string(p));
   if (p.kind == kTma) return launch_tma(p, a, fn, dev, stream, flags);
+  // The instance that triggers once its loads are issued (warp, CTA and
+  // cluster kinds; the two-pass kernel has none and triggers after its
+  // reduction instead).
+  Plan pt = p;
+  pt.trig_loads = p.kind != kTwoPass;
+  KernelFn fn_tl = pt.trig_loads ? pick_kernel(dtype, pt, var) : fn;
   // Rows handled per CTA-group in grid.x; split very tall problems into launches.
   const int64_t rows_per_unit = p.kind == kWarpRows ? p.rows_per_cta : 1;  // rows per CTA
   const bool clustered = p.kind == kClusterRows || (p.kind == kTwoPass && p.cluster > 1);
   const int64_t ctas_per_unit = clustered ? p.cluster : 1;
   const int64_t max_rows = (kMaxGridX / ctas_per_unit) * rows_per_unit;
   const int threads = p.kind == kWarpRows ? p.rows_per_cta * p.tpr : p.tpr;
-  const int64_t wave = p.prefetch == kPrefetchFirstWave || p.prefetch == kPrefetchAhead
-                           ? first_wave_ctas(dev, reinterpret_cast<const void*>(fn), threads)
-                           : 0;
+  const bool need_wave =
+      p.prefetch == kPrefetchFirstWave || p.prefetch == kPrefetchAhead || p.early < 0;
+  const int64_t wave = need_wave ? first_wave_ctas(dev, reinterpret_cast<const void*>(fn), threads)
+                                 : 0;
   a.prefetch_ctas = p.prefetch == kPrefetchAll ? INT64_MAX : wave;
   // The row the CTA one wave later handles: a wave of CTAs covers wave /
   // ctas_per_unit row units of rows_per_unit rows.
@@ -881,6 +912,14 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     cfg.gridDim = dim3(static_cast<unsigned>(units * ctas_per_unit), 1, 1);
+    // Trigger point by default: once the loads are issued when the grid has
+    // more than one wave (the last wave's trigger then lets the next grid's
+    // CTAs start and prefetch while this grid's last CTAs finish), after the
+    // row reduction when it fits one wave (an earlier trigger there only
+    // parks the next grid's CTAs on the SMs: decode batches ran up to 10%
+    // slower with it).
+    c.early_trigger = p.early >= 0 ? p.early : (units * ctas_per_unit > wave ? 2 : 1);
+    KernelFn f = c.early_trigger == 2 ? fn_tl : fn;
     cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
@@ -898,7 +937,7 @@ int launch(const Plan& p, RmsArgs a, int dtype, const Variant& var, const Device
       attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
       ++cfg.numAttrs;
     }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, c);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, f, c);
     if (e != cudaSuccess)
       return fail(HPRN_ERR_CUDA, std::string("rms_norm launch failed (") + plan_string(p) +
                                      "): " + cudaGetErrorString(e));

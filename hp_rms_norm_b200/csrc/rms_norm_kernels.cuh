@@ -110,8 +110,12 @@ struct RmsArgs {
   // the row this many rows ahead, the row of the CTA that will take its place
   // one wave later.
   int64_t prefetch_ahead_rows;
-  // Nonzero: trigger dependents (pdl_trigger) right after the row reduction
-  // instead of after the last store.
+  // Where a CTA triggers its dependents (pdl_trigger): 0 after its last
+  // store, 1 after the row reduction.  Triggering once the loads (and
+  // prefetches) are issued is a separate kernel instance (template TL), not
+  // this runtime value: with the trigger compiled in that early, even
+  // untaken, short single-wave launches ran up to 15% slower.  Instances
+  // without TL treat 2 as 1.
   int32_t early_trigger;
 };
 
@@ -450,7 +454,7 @@ __host__ __device__ constexpr bool hold_products(bool res, int vpt) { return res
 // lanes.  No shared memory, no block barrier.  Lanes past the last row stay
 // in the warp (their loads and stores are skipped) so every shuffle has all
 // 32 lanes.
-template <typename T, int VEC, int VPT, bool RES, int OUT>
+template <typename T, int VEC, int VPT, bool RES, int OUT, bool TL>
 __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   constexpr int EPV = Vec<VEC>::kElems;
   const int lpr = a.lanes_per_row;
@@ -477,6 +481,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
     }
   }
   if (active && sub == 0) prefetch_row_ahead<VEC, RES>(a, row, 0, a.nvec);
+  if constexpr (TL) pdl_trigger();
   float a0 = 0.f, a1 = 0.f;
   // Dynamic fp8: max |r * w| does not depend on inv, so it is reduced next to
   // the sum of squares and scaled by inv once (see prod_amax).  The products
@@ -516,7 +521,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
   }
   float inv_scale = static_inv_scale<OUT>(a);
   const float inv = rsqrtf(fmaf(lane_group_sum(a0 + a1, lpr), a.inv_hidden, a.eps));
-  if (a.early_trigger) pdl_trigger();
+  if (!TL && a.early_trigger >= 1) pdl_trigger();
   if constexpr (OUT == kOutFp8Dynamic) {
     const float scale = fmaxf(lane_group_max(m, lpr) * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
@@ -534,7 +539,7 @@ __global__ void __launch_bounds__(256) rms_norm_warp_rows(RmsArgs a) {
                              inv_scale);
     }
   }
-  if (!a.early_trigger) pdl_trigger();
+  if (!TL && a.early_trigger == 0) pdl_trigger();
 }
 
 // Largest CTA a cta/cluster kernel with VPT vectors per thread is compiled
@@ -570,10 +575,11 @@ __host__ __device__ constexpr bool cta_has_knobs(bool res, int out, int vpt) {
   return res || (out != kOutNvfp4 && out != kOutFp8Group) || vpt < 4;
 }
 
-template <typename T, int VEC, int VPT, bool CLUSTER, bool RES, int OUT>
+template <typename T, int VEC, int VPT, bool CLUSTER, bool RES, int OUT, bool TL>
 __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUSTER, RES, OUT))
     rms_norm_cta_rows(RmsArgs a) {
   constexpr bool kKnobs = cta_has_knobs(RES, OUT, VPT);
+  static_assert(kKnobs || !TL, "the knob-less instances trigger at their end only");
   constexpr int EPV = Vec<VEC>::kElems;
   __shared__ float warp_part[32];
   __shared__ float warp_amax[32];
@@ -621,6 +627,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
     }
   }
   if (kKnobs && tid == 0) prefetch_row_ahead<VEC, RES>(a, row, v_begin, v_end);
+  if constexpr (TL) pdl_trigger();
   // Dynamic fp8: max |r * w| does not depend on inv, so it travels with the
   // sum of squares through the same barrier (and cluster phase) and is scaled
   // by inv once at the end (see prod_amax).  The products r * w are held
@@ -680,7 +687,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
     if constexpr (kAmax) amax = warp_max(lane < static_cast<int>(csize) ? cta_amax[lane] : 0.f);
   }
   const float inv = rsqrtf(fmaf(total, a.inv_hidden, a.eps));
-  if (kKnobs && a.early_trigger) pdl_trigger();
+  if (kKnobs && !TL && a.early_trigger >= 1) pdl_trigger();
   if constexpr (kAmax) {
     const float scale = fmaxf(amax * inv, kMinAmax) / kE4m3Max;
     inv_scale = 1.0f / scale;
@@ -698,7 +705,7 @@ __global__ void __launch_bounds__(cta_max_threads(VPT), cta_min_blocks(VPT, CLUS
                              inv_scale);
     }
   }
-  if (!kKnobs || !a.early_trigger) pdl_trigger();
+  if (!kKnobs || (!TL && a.early_trigger == 0)) pdl_trigger();
 }
 
 // ---------------------------------------------------------------------------

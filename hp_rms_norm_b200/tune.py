@@ -258,7 +258,7 @@ def sweep(rows: int, hiddens: list[int], dtype: str = "bf16", warm: bool = False
     return results
 
 
-KNOBS = [f"default:pf{pf}:et{et}" for pf in (0, 1, 2, 3) for et in (0, 1)]
+KNOBS = [f"default:pf{pf}:et{et}" for pf in (0, 1, 2, 3) for et in (0, 1, 2)]
 
 
 def knob_sweep(a, reps: int = 3) -> None:

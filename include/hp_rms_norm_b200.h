@@ -241,8 +241,8 @@ HPRN_API int hprn_rms_norm_plan(int64_t rows, int64_t hidden, int dtype, const v
  * for its first rows before waiting on the preceding grid (0 none, 1 the
  * grid's first wave of CTAs, 2 every CTA, 3 the first wave, with every CTA also
  * prefetching the row of the CTA one wave later) and E where dependents are triggered
- * (0 after the last store, 1 after the row reduction); without them the plan's
- * defaults apply.  "default:pf<F>:et<E>" keeps the built-in plan and sets only
+ * (0 after the last store, 1 after the row reduction, 2 once the loads are
+ * issued); without them the plan's defaults apply.  "default:pf<F>:et<E>" keeps the built-in plan and sets only
  * the knobs.  hprn_rms_norm_plan echoes knobs an override names.  The
  * HP_RMS_NORM_PLAN environment variable, read at
  * the first call, sets the same override.  A forced plan that does not fit a

@@ -195,7 +195,7 @@ def test_plan_override_parsing():
 
 
 @pytest.mark.parametrize("bad", [
-    "default:pf4:et0", "default:pf1:et2", "default:pf1", "default:pf1:et1x",
+    "default:pf4:et0", "default:pf1:et3", "default:pf1", "default:pf1:et1x",
     "cta:vec32:vpt1:tpr256:cluster1:rpc1:pf1", "cta:vec32:vpt1:tpr256:cluster1:rpc1:pf-1:et0",
     "cta:vec32:vpt1:tpr256:cluster1:rpc1 ", "cta:vec32:vpt1:tpr256:cluster1:rpc1:et1:pf1",
 ])

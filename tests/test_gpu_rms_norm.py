@@ -449,7 +449,7 @@ def test_pdl_chains_match_plain_launches(cuda, hidden):
             assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
-KNOBS = [f"default:pf{pf}:et{et}" for pf in (0, 1, 2, 3) for et in (0, 1)]
+KNOBS = [f"default:pf{pf}:et{et}" for pf in (0, 1, 2, 3) for et in (0, 1, 2)]
 
 
 @pytest.mark.parametrize("knobs", KNOBS)

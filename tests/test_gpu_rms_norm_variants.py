@@ -114,7 +114,7 @@ def test_variant_every_plan_kind(cuda, variant, rows, hidden, plan):
         capi.set_plan_override(None)
 
 
-@pytest.mark.parametrize("knobs", [f"default:pf{pf}:et{et}" for pf in (0, 1, 2, 3) for et in (0, 1)])
+@pytest.mark.parametrize("knobs", [f"default:pf{pf}:et{et}" for pf in (0, 1, 2, 3) for et in (0, 1, 2)])
 @pytest.mark.parametrize("rows,hidden", [(600, 4096), (300, 32768)])
 @pytest.mark.parametrize("variant", VARIANTS)
 def test_variant_launch_knobs_keep_results(cuda, variant, rows, hidden, knobs):
