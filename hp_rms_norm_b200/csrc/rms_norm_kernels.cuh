@@ -32,8 +32,10 @@
 //   * streamed rows are marked L2 evict_first, the weight row evict_last;
 //   * a CTA's first rows are bulk-prefetched into L2 before it waits on the
 //     preceding grid (programmatic dependent launch), so their DRAM reads
-//     overlap that grid's drain; dependents are triggered after the row
-//     reduction (both are per-plan launch knobs, see default_knobs);
+//     overlap that grid's drain, and each CTA also prefetches the row of the
+//     CTA one wave after it; dependents are triggered once the loads are
+//     issued in grids of more than one wave (template TL), after the row
+//     reduction otherwise (per-plan launch knobs, see default_knobs);
 //   * the row is held by part of a warp or one warp (short rows, no shared
 //     memory or block barrier at all), one CTA, or a thread-block cluster of
 //     up to 8 CTAs
