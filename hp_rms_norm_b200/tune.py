@@ -18,8 +18,9 @@ cluster per row) past 4096 vectors, and TMA-staged rows (unless
 times the default plan under each pair of launch knobs instead
 (``default:pf<p>:et<e>``: L2 prefetch before the programmatic-launch wait in
 no CTA, the first wave or every CTA, or the first wave with every CTA also
-prefetching the row one wave ahead; dependents triggered after the last store
-or after the row reduction), one process per pair, which is how
+prefetching the row one wave ahead; dependents triggered after the last store,
+after the row reduction, or once the loads are issued), one process per pair,
+which is how
 ``default_knobs`` in csrc/rms_norm.cu was fitted.  Timing: a CUDA graph of
 back-to-back launches over
 rotating buffer sets of at least 600 MB, so every launch reads cold data (or
