@@ -118,12 +118,16 @@ __global__ void __launch_bounds__(256) act_and_mul_rows(ActArgs a) {
       u[k] = ld_stream<VEC>(up + i * EPV, pol);
     }
   }
+  // Dependents are triggered once the loads are issued (they still wait for
+  // this grid to complete before reading): GELU at 512 x 14336 in 10.01
+  // against 10.63 us with the trigger after the last store, 58.95 against
+  // 59.82 at 4096 x 14336.
+  pdl_trigger();
 #pragma unroll
   for (int k = 0; k < U; ++k) {
     const int64_t i = base + static_cast<int64_t>(k) * blockDim.x;
     if (i < a.nvec) st_global<VEC>(dst + i * EPV, act_mul<T, VEC, ACT>(g[k], u[k]));
   }
-  pdl_trigger();
 }
 
 using ActFn = void (*)(ActArgs);

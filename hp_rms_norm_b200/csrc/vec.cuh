@@ -405,12 +405,14 @@ __device__ __forceinline__ uint32_t e2m1x8(float2 a, float2 b, float2 c, float2 
 // Programmatic dependent launch.  pdl_wait() before the kernel's first
 // global-memory load or store (only L2 prefetches come before it): blocks
 // until the grid this one depends on (if it was launched that way) has
-// completed and its memory is visible.  pdl_trigger() once a CTA's row
-// reductions are done (or after its last store; a launch knob): a following
-// kernel launched with programmatic stream serialization may then be scheduled
-// once every CTA of this grid has reached it (or exited), so its launch and its
-// L2 prefetch overlap this grid's epilogue and drain; it still reads nothing
-// before this grid has completed.  Triggering at kernel entry instead let the
+// completed and its memory is visible.  pdl_trigger() once a CTA's loads are
+// issued (elementwise kernels, and row kernels in grids of more than one
+// wave) or once its row reduction is done (single-wave row grids; after the
+// last store is a launch knob): a following kernel launched with programmatic
+// stream serialization may then be scheduled once every CTA of this grid has
+// reached it (or exited), so its launch and its L2 prefetch overlap this
+// grid's epilogue and drain; it still reads nothing before this grid has
+// completed.  Triggering at kernel entry instead let the
 // next grid's CTAs take SM slots and wait while this grid was still running:
 // single-wave launches (decode batches) then took up to 40% longer than with no
 // programmatic launch at all.  With no programmatic dependency both are no-ops.
